@@ -1,0 +1,111 @@
+/*
+ * qwen_b200.h - C ABI of the B200-native Qwen3-0.6B fp16 greedy-decode engine.
+ *
+ * Plain C types only: raw device pointers, sizes, a cudaStream_t passed as
+ * void*.  No torch types.  The two decode launchers keep the exact symbol
+ * names and parameter order of the upstream launchers they replace, so an
+ * existing binding (Tools/megakernel/qwen_ops.cpp:9-27) links against this
+ * library unchanged.
+ *
+ * All device pointers must be 16-byte aligned (the weights are streamed with
+ * bulk async copies).  All launchers are asynchronous on `stream`; argument
+ * errors found on the host are reported through qwen_b200_last_error(), and
+ * errors found on the device (a bounded wait that ran out, a misaligned weight
+ * pointer in the packed table) through qwen_b200_device_status() and a -1 in
+ * the token output.
+ *
+ * Calls that share a device must not overlap in time: they share one
+ * per-device workspace (as the upstream launchers share their static device
+ * state, megakernel.cu:714-737).
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Per-layer weight table, 12 pointers = 96 bytes, 16-byte aligned.
+ * Same field order as the upstream struct (megakernel.cu:87-100) and the
+ * upstream packer (Model/Qwen06B_architecture.py:177-202). */
+typedef struct __attribute__((aligned(16))) LDGLayerWeight {
+  const void *input_layernorm_weight;     /* [1024]        */
+  const void *q_proj_weight;              /* [2048, 1024]  */
+  const void *k_proj_weight;              /* [1024, 1024]  */
+  const void *v_proj_weight;              /* [1024, 1024]  */
+  const void *q_norm_weight;              /* [128]         */
+  const void *k_norm_weight;              /* [128]         */
+  const void *o_proj_weight;              /* [1024, 2048]  */
+  const void *post_attn_layernorm_weight; /* [1024]        */
+  const void *gate_proj_weight;           /* [3072, 1024]  */
+  const void *up_proj_weight;             /* [3072, 1024]  */
+  const void *down_proj_weight;           /* [1024, 3072]  */
+  const void *padding;                    /* zero          */
+} LDGLayerWeight;
+
+/* ABI version of the packed table + launcher signatures
+ * (Tools/megakernel/qwen_ops.cpp:30-32; Model/Qwen06B_architecture.py:12). */
+#define QWEN_B200_ABI_VERSION 2
+int qwen_b200_abi_version(void);
+
+/*
+ * One greedy decode step: embed(input_token_id) -> num_layers layers at
+ * `position` (writes K/V at that position) -> final RMSNorm (fp32 into
+ * g_normalized) -> tied lm_head -> argmax into *output_token_id (device int).
+ * Replaces launch_ldg_decode_direct, Tools/megakernel/megakernel.cu:1150-1196
+ * (same name, same parameters).  Scratch buffers keep the upstream dtypes and
+ * sizes (Model/Qwen06B_architecture.py:240-255); after the call g_normalized
+ * holds the final normalised hidden (fp32[1024]) and hidden_buffer the last
+ * layer's output (fp16[1024]).  stream is a cudaStream_t.
+ */
+void launch_ldg_decode_direct(
+    int input_token_id, int *output_token_id, const void *embed_weight,
+    const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table, void *k_cache,
+    void *v_cache, void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+    void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate, void *g_normalized,
+    void *block_max_vals, void *block_max_idxs, int num_layers, int position, int max_seq_len,
+    float attn_scale, void *stream);
+
+/*
+ * num_steps greedy steps from first_token_id at start_position, the produced
+ * token fed back on the device; output_log[s] = token produced at step s.
+ * One kernel launch for all steps, no host round trip.
+ * Replaces launch_ldg_generate_nosync, Tools/megakernel/megakernel.cu:1247-1314
+ * (same name, same parameters).
+ */
+void launch_ldg_generate_nosync(
+    int first_token_id, int num_steps, const void *embed_weight,
+    const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table, void *k_cache,
+    void *v_cache, void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+    void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate, void *g_normalized,
+    void *block_max_vals, void *block_max_idxs, int *output_log, int num_layers,
+    int start_position, int max_seq_len, float attn_scale, void *stream);
+
+/* Error reporting (no upstream counterpart: the upstream megakernel launchers
+ * return void and check no CUDA errors, qwen_ops.cpp:34-165).
+ * qwen_b200_last_error: 0 if the calling thread's last launcher call was
+ * accepted, else a nonzero code; a message is copied into msg (may be NULL).
+ * qwen_b200_device_status: synchronises the device's work submitted so far,
+ * then returns the device-side status word of the last decode launch on
+ * `device` (0 = ok; else (code, where) packed as described in the source). */
+int qwen_b200_last_error(char *msg, int msg_len);
+int qwen_b200_device_status(int device, uint64_t *detail);
+
+/* Wall-clock limit for every bounded wait inside the decode kernel,
+ * nanoseconds (default 2e9).  Applies to later launches on all devices. */
+void qwen_b200_set_wait_timeout_ns(long long ns);
+
+/* Failure-detection self test: launches one tiny kernel whose thread waits,
+ * with the decode kernel's own bounded-wait routine, on a handoff word that
+ * nothing writes.  Returns the status code that wait produced (the timeout
+ * code when the bound works).  Synchronous. */
+int qwen_b200_selftest_wait_timeout(long long timeout_ns, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN_B200_H */

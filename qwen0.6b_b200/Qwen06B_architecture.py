@@ -1,0 +1,260 @@
+"""Weight loading and high-level decode API for Qwen3-0.6B (B200 engine).
+
+Drop-in counterpart of the upstream ``Model/Qwen06B_architecture.py``: the
+same module constants, ``EXTENSION_ABI_VERSION``, ``load_weights``,
+``_pack_layer_weights``, ``Decoder`` (``step`` / ``generate`` / ``reset`` /
+``position``) and ``generate``, driving the ``qwen_megakernel_C`` extension
+built from this package (``build.py``).  There is no CPU fallback: importing
+this module without the built CUDA extension raises, as upstream does
+(``Model/Qwen06B_architecture.py:31-94``).
+
+Differences from upstream, all deliberate:
+* misaligned weight or scratch pointers raise ``RuntimeError`` instead of
+  being printed (the B200 kernel streams weights with 16-byte bulk copies);
+* ``step`` raises if the device reports a failed launch (a -1 token), and
+  ``generate`` likewise;
+* ``load_weights("synthetic[:seed]")`` returns seeded random-init weights of
+  the real architecture (``qwen_weights.synthetic_weights``); any other name
+  goes to HF ``from_pretrained`` exactly as upstream;
+* ``Decoder.generate_ids`` takes token ids and returns token ids, for callers
+  without a tokenizer.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+if _HERE not in sys.path:
+    sys.path.insert(0, _HERE)
+
+try:
+    import qwen_megakernel_C
+except ImportError:
+    qwen_megakernel_C = None
+
+from qwen_weights import (HEAD_DIM, HIDDEN_SIZE, INTERMEDIATE_SIZE, KV_SIZE, MAX_SEQ_LEN,  # noqa: E402
+                          NUM_KV_HEADS, NUM_LAYERS, Q_SIZE, ROPE_THETA, VOCAB_SIZE,
+                          rope_tables, synthetic_weights)
+
+EXTENSION_ABI_VERSION = 2
+
+__all__ = ["EXTENSION_ABI_VERSION", "NUM_LAYERS", "NUM_KV_HEADS", "HEAD_DIM", "HIDDEN_SIZE",
+           "INTERMEDIATE_SIZE", "Q_SIZE", "KV_SIZE", "MAX_SEQ_LEN", "VOCAB_SIZE", "ROPE_THETA",
+           "load_weights", "Decoder", "generate"]
+
+
+def _require_megakernel_op(op_name: str):
+    """Return an op from the extension module (upstream :31-60)."""
+    if qwen_megakernel_C is not None and hasattr(qwen_megakernel_C, op_name):
+        return getattr(qwen_megakernel_C, op_name)
+    namespace = getattr(torch.ops, "qwen_megakernel_C", None)
+    if namespace is not None and hasattr(namespace, op_name):
+        return getattr(namespace, op_name)
+    raise RuntimeError(
+        f"qwen_megakernel_C op '{op_name}' is unavailable: the B200 CUDA extension is not "
+        f"built or not loadable for torch {torch.__version__}. Build it with "
+        f"`python {os.path.join(_HERE, 'build.py')}`.")
+
+
+def _assert_extension_compatibility() -> None:
+    """Fail fast on a stale extension binary (upstream :63-91)."""
+    if qwen_megakernel_C is None:
+        return
+    try:
+        ext_abi = int(qwen_megakernel_C.abi_version())
+    except Exception:
+        ext_abi = None
+    if ext_abi != EXTENSION_ABI_VERSION:
+        built = getattr(qwen_megakernel_C, "built_torch_version", lambda: "unknown")()
+        raise RuntimeError(
+            f"Incompatible qwen_megakernel_C extension: expected ABI {EXTENSION_ABI_VERSION}, "
+            f"got {ext_abi} (built against torch {built}); rebuild it.")
+
+
+_assert_extension_compatibility()
+_decode = _require_megakernel_op("decode")
+
+
+def load_weights(model_name: str = "Qwen/Qwen3-0.6B", verbose: bool = True):
+    """Weights dict + tokenizer, in the upstream layout (upstream :97-174).
+
+    ``model_name`` of the form ``"synthetic"`` or ``"synthetic:<seed>"`` gives
+    seeded random-init weights and no tokenizer.
+    """
+    if model_name.startswith("synthetic"):
+        seed = int(model_name.split(":", 1)[1]) if ":" in model_name else 0
+        return synthetic_weights(seed=seed, device="cuda"), None
+
+    from transformers import AutoModelForCausalLM, AutoTokenizer
+
+    if verbose:
+        print(f"Loading {model_name}...")
+    model = AutoModelForCausalLM.from_pretrained(model_name, torch_dtype=torch.float16,
+                                                 device_map="cuda")
+    tokenizer = AutoTokenizer.from_pretrained(model_name)
+    state = model.state_dict()
+    cos_table, sin_table = (t.cuda() for t in rope_tables(MAX_SEQ_LEN))
+    layer_weights = []
+    for i in range(NUM_LAYERS):
+        p = f"model.layers.{i}."
+        layer_weights.extend([
+            state[p + "input_layernorm.weight"].contiguous(),
+            state[p + "self_attn.q_proj.weight"].contiguous(),
+            state[p + "self_attn.k_proj.weight"].contiguous(),
+            state[p + "self_attn.v_proj.weight"].contiguous(),
+            state[p + "self_attn.q_norm.weight"].contiguous(),
+            state[p + "self_attn.k_norm.weight"].contiguous(),
+            state[p + "self_attn.o_proj.weight"].contiguous(),
+            state[p + "post_attention_layernorm.weight"].contiguous(),
+            state[p + "mlp.gate_proj.weight"].contiguous(),
+            state[p + "mlp.up_proj.weight"].contiguous(),
+            state[p + "mlp.down_proj.weight"].contiguous(),
+        ])
+    embed_weight = state["model.embed_tokens.weight"].contiguous()
+    weights = dict(embed_weight=embed_weight, layer_weights=layer_weights,
+                   final_norm_weight=state["model.norm.weight"].contiguous(),
+                   lm_head_weight=embed_weight, cos_table=cos_table, sin_table=sin_table)
+    del model
+    torch.cuda.empty_cache()
+    return weights, tokenizer
+
+
+_FIELD_NAMES = ("input_layernorm", "q_proj", "k_proj", "v_proj", "q_norm", "k_norm", "o_proj",
+                "post_attn_norm", "gate_proj", "up_proj", "down_proj")
+
+
+def _pack_layer_weights(layer_weights: list) -> torch.Tensor:
+    """int64 device tensor of 12 pointers per layer (11 weights + zero pad),
+    16-byte aligned: the LDGLayerWeight table (upstream :177-202)."""
+    n = len(_FIELD_NAMES)
+    n_layers = len(layer_weights) // n
+    if n_layers < 1 or len(layer_weights) != n_layers * n:
+        raise ValueError(f"expected {n} weight tensors per layer, got {len(layer_weights)}")
+    bad = []
+    ptrs = []
+    for li in range(n_layers):
+        for j in range(n):
+            t = layer_weights[li * n + j]
+            if not (t.is_cuda and t.dtype == torch.float16 and t.is_contiguous()):
+                raise ValueError(f"layer {li} {_FIELD_NAMES[j]}: need a contiguous CUDA fp16 tensor")
+            if t.data_ptr() % 16:
+                bad.append(f"layer {li} {_FIELD_NAMES[j]} ptr={t.data_ptr():#x}")
+            ptrs.append(t.data_ptr())
+        ptrs.append(0)
+    if bad:
+        raise RuntimeError("misaligned weight tensors (16-byte alignment required): " + "; ".join(bad))
+    dev = layer_weights[0].device
+    t = torch.zeros(len(ptrs) + 2, dtype=torch.int64, device=dev)
+    off = ((16 - t.data_ptr() % 16) % 16) // 8
+    t_al = t[off: off + len(ptrs)]
+    t_al.copy_(torch.tensor(ptrs, dtype=torch.int64))
+    assert t_al.data_ptr() % 16 == 0
+    return t_al
+
+
+class Decoder:
+    """Stateful decoder over the B200 persistent decode kernel (upstream :205-382)."""
+
+    def __init__(self, weights=None, tokenizer=None, model_name="Qwen/Qwen3-0.6B",
+                 verbose: bool = True, num_layers: int | None = None):
+        if weights is None:
+            weights, tokenizer = load_weights(model_name, verbose=verbose)
+        self.tokenizer = tokenizer
+        self._position = 0
+        self._weights = weights  # keep alive: the packed table holds raw pointers
+        self._embed_weight = weights["embed_weight"]
+        self._final_norm_weight = weights["final_norm_weight"]
+        self._lm_head_weight = weights["lm_head_weight"]
+        self._cos_table = weights["cos_table"]
+        self._sin_table = weights["sin_table"]
+        lw = weights["layer_weights"]
+        self._num_layers = num_layers or len(lw) // 11
+        self._layer_weights_packed = _pack_layer_weights(lw[: self._num_layers * 11])
+        self._attn_scale = 1.0 / math.sqrt(HEAD_DIM)
+        dev = self._embed_weight.device
+        self._k_cache = torch.zeros(self._num_layers, NUM_KV_HEADS, MAX_SEQ_LEN, HEAD_DIM,
+                                    dtype=torch.float16, device=dev)
+        self._v_cache = torch.zeros_like(self._k_cache)
+        f16 = dict(dtype=torch.float16, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        self._hidden = torch.empty(HIDDEN_SIZE, **f16)
+        self._act = torch.empty(Q_SIZE, **f32)
+        self._res = torch.empty(HIDDEN_SIZE, **f32)
+        self._q = torch.empty(Q_SIZE, **f16)
+        self._k = torch.empty(KV_SIZE, **f16)
+        self._v = torch.empty(KV_SIZE, **f16)
+        self._attn_out = torch.empty(Q_SIZE, **f16)
+        self._mlp_inter = torch.empty(INTERMEDIATE_SIZE, **f32)
+        self._norm_out = torch.empty(HIDDEN_SIZE, **f32)
+        self._fmax_vals = torch.empty(4096, **f32)
+        self._fmax_idxs = torch.empty(4096, **i32)
+        self._out_token = torch.empty(1, **i32)
+
+    def _args(self):
+        return (self._embed_weight, self._layer_weights_packed, self._final_norm_weight,
+                self._lm_head_weight, self._cos_table, self._sin_table, self._k_cache,
+                self._v_cache, self._hidden, self._act, self._res, self._q, self._k, self._v,
+                self._attn_out, self._mlp_inter, self._norm_out, self._fmax_vals,
+                self._fmax_idxs)
+
+    def _raise_device_failure(self, what: str) -> None:
+        status = int(qwen_megakernel_C.device_status(self._embed_weight.device.index or 0))
+        raise RuntimeError(f"{what}: device-side failure, status word {status:#x}")
+
+    def step(self, input_token_id: int | torch.Tensor) -> int:
+        """Decode one token at the current position; returns the greedy next token."""
+        result = _decode(int(input_token_id), *self._args(), self._num_layers, self._position,
+                         MAX_SEQ_LEN, self._attn_scale)
+        self._out_token.copy_(result)
+        tok = int(result.item())
+        if tok < 0:
+            self._raise_device_failure("Decoder.step")
+        self._position += 1
+        return tok
+
+    def reset(self):
+        self._position = 0
+        self._k_cache.zero_()
+        self._v_cache.zero_()
+
+    @property
+    def position(self) -> int:
+        return self._position
+
+    def generate_ids(self, ids: list[int], max_tokens: int = 100, reset: bool = True) -> list[int]:
+        """Prefill ids[:-1] with step(), then generate_nosync from ids[-1]."""
+        if reset:
+            self.reset()
+        for tid in ids[:-1]:
+            self.step(tid)
+        out = self.generate_nosync(ids[-1], max_tokens).cpu().tolist()
+        if any(t < 0 for t in out):
+            self._raise_device_failure("Decoder.generate_ids")
+        return out
+
+    def generate_nosync(self, first_token: int, num_steps: int) -> torch.Tensor:
+        """Device-resident greedy loop from the current position; int32[num_steps] on device."""
+        gen = _require_megakernel_op("generate_nosync")
+        out = gen(int(first_token), int(num_steps), *self._args(), self._num_layers,
+                  self._position, MAX_SEQ_LEN, self._attn_scale)
+        self._position += num_steps
+        return out
+
+    def generate(self, prompt: str, max_tokens: int = 100) -> str:
+        self.reset()
+        ids = self.tokenizer.encode(prompt, add_special_tokens=True)
+        out = self.generate_ids(ids, max_tokens, reset=False)
+        eos = self.tokenizer.eos_token_id
+        if eos in out:
+            out = out[: out.index(eos)]
+        return self.tokenizer.decode(out, skip_special_tokens=True)
+
+
+def generate(prompt: str, max_tokens: int = 50, verbose: bool = True) -> str:
+    """One-shot convenience: load model, generate, return text (upstream :385-387)."""
+    return Decoder(verbose=verbose).generate(prompt, max_tokens)

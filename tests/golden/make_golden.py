@@ -1,0 +1,182 @@
+"""Generate golden fixtures from the upstream implementation itself.
+
+Runs on a CUDA box.  It loads the upstream extension modules built from the
+unmodified upstream sources by ``oracle/build_ref.py`` (``oracle/_ref/``:
+``qwen_megakernel_C``, ``rmsnorm``, ``swiglu_fused``) and records their
+outputs on seeded inputs:
+
+* ``ref_decode_*.npz``: greedy decode through the upstream
+  ``qwen_megakernel_C.decode`` / ``generate_nosync`` ops with the buffers the
+  upstream ``Decoder`` allocates (``Model/Qwen06B_architecture.py:220-255``),
+  weights from ``qwen_weights.synthetic_weights(seed, num_layers)``; per step
+  the input token, position, output token, ``norm_out`` (the fp32 final-normed
+  hidden the upstream kernel leaves in that buffer), the fp16 ``hidden`` and
+  the K/V cache rows written at that position for the first and last layer;
+* ``ref_longctx_*.npz``: the same at positions 1920.. with a seeded random
+  KV cache already holding positions 0..1919 (attention over ~1.9k tokens);
+* ``ref_ops.npz``: ``rmsnorm.forward`` (simple and fused-residual) and
+  ``swiglu_fused.forward`` / ``forward_down`` on seeded inputs.
+
+Usage: ``python tests/golden/make_golden.py --out tests/golden``.
+The inputs are regenerated from the seeds by ``tests/golden/inputs.py``; only
+outputs are stored.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import math
+import os
+import sys
+import time
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "qwen0.6b_b200"))
+sys.path.insert(0, HERE)
+
+from inputs import DECODE_CASES, LONGCTX_CASES, OPS_CASE, longctx_cache, ops_inputs  # noqa: E402
+from qwen_weights import synthetic_weights  # noqa: E402
+
+
+def _load_ref(name: str):
+    path = os.path.join(ROOT, "oracle", "_ref", f"{name}.so")
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _pack(layer_weights, dev):
+    ptrs = []
+    for li in range(len(layer_weights) // 11):
+        ptrs += [t.data_ptr() for t in layer_weights[li * 11: li * 11 + 11]] + [0]
+    t = torch.zeros(len(ptrs) + 2, dtype=torch.int64, device=dev)
+    off = ((16 - t.data_ptr() % 16) % 16) // 8
+    t = t[off: off + len(ptrs)]
+    t.copy_(torch.tensor(ptrs, dtype=torch.int64))
+    return t
+
+
+class RefDecoder:
+    """The upstream Decoder's buffers, driving the upstream ops directly."""
+
+    def __init__(self, mk, seed, num_layers, dev="cuda"):
+        self.mk = mk
+        self.L = num_layers
+        w = synthetic_weights(seed=seed, num_layers=num_layers, device=dev)
+        self.w = w
+        self.packed = _pack(w["layer_weights"], dev)
+        f16, f32, i32 = (dict(dtype=d, device=dev) for d in (torch.float16, torch.float32, torch.int32))
+        self.kc = torch.zeros(num_layers, 8, 2048, 128, **f16)
+        self.vc = torch.zeros_like(self.kc)
+        self.bufs = [torch.empty(1024, **f16), torch.empty(2048, **f32), torch.empty(1024, **f32),
+                     torch.empty(2048, **f16), torch.empty(1024, **f16), torch.empty(1024, **f16),
+                     torch.empty(2048, **f16), torch.empty(3072, **f32), torch.empty(1024, **f32),
+                     torch.empty(4096, **f32), torch.empty(4096, **i32)]
+        self.scale = 1.0 / math.sqrt(128)
+
+    def _args(self):
+        w = self.w
+        return (w["embed_weight"], self.packed, w["final_norm_weight"], w["lm_head_weight"],
+                w["cos_table"], w["sin_table"], self.kc, self.vc, *self.bufs)
+
+    def step(self, tok, pos):
+        out = self.mk.decode(int(tok), *self._args(), self.L, int(pos), 2048, self.scale)
+        torch.cuda.synchronize()
+        return int(out.item())
+
+    def gen(self, tok, pos, n):
+        out = self.mk.generate_nosync(int(tok), int(n), *self._args(), self.L, int(pos), 2048,
+                                      self.scale)
+        torch.cuda.synchronize()
+        return out.cpu().numpy()
+
+    @property
+    def hidden(self):
+        return self.bufs[0]
+
+    @property
+    def norm_out(self):
+        return self.bufs[8]
+
+
+def record_steps(dec, toks, pos0):
+    rec = dict(inp=[], pos=[], out=[], norm=[], hidden=[], k_first=[], v_first=[], k_last=[], v_last=[])
+    for i, t in enumerate(toks):
+        pos = pos0 + i
+        o = dec.step(t, pos)
+        rec["inp"].append(t)
+        rec["pos"].append(pos)
+        rec["out"].append(o)
+        rec["norm"].append(dec.norm_out.cpu().numpy().copy())
+        rec["hidden"].append(dec.hidden.view(torch.int16).cpu().numpy().copy())
+        for tag, li in (("first", 0), ("last", dec.L - 1)):
+            rec["k_" + tag].append(dec.kc[li, :, pos].view(torch.int16).cpu().numpy().copy())
+            rec["v_" + tag].append(dec.vc[li, :, pos].view(torch.int16).cpu().numpy().copy())
+    return {k: np.asarray(v) for k, v in rec.items()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=HERE)
+    args = ap.parse_args()
+    os.makedirs(args.out, exist_ok=True)
+    mk = _load_ref("qwen_megakernel_C")
+    for case in DECODE_CASES:
+        t0 = time.time()
+        dec = RefDecoder(mk, case["seed"], case["num_layers"])
+        rec = record_steps(dec, case["prompt"], 0)
+        gen = dec.gen(case["prompt"][-1], len(case["prompt"]) - 1, case["gen_steps"]) \
+            if case["gen_steps"] else np.zeros(0, np.int32)
+        # generate_nosync re-ran the last prompt position: positions
+        # len-1 .. len-2+gen_steps; the final norm_out is that of the last step.
+        np.savez_compressed(os.path.join(args.out, f"ref_decode_{case['name']}.npz"),
+                            gen=gen, gen_norm=dec.norm_out.cpu().numpy(), **rec)
+        print(f"decode {case['name']}: {time.time() - t0:.1f}s tokens={rec['out'].tolist()} gen={gen.tolist()}")
+        del dec
+        torch.cuda.empty_cache()
+    for case in LONGCTX_CASES:
+        t0 = time.time()
+        dec = RefDecoder(mk, case["seed"], case["num_layers"])
+        kc, vc = longctx_cache(case)
+        dec.kc.copy_(kc.cuda())
+        dec.vc.copy_(vc.cuda())
+        rec = record_steps(dec, case["tokens"], case["start"])
+        np.savez_compressed(os.path.join(args.out, f"ref_longctx_{case['name']}.npz"), **rec)
+        print(f"longctx {case['name']}: {time.time() - t0:.1f}s tokens={rec['out'].tolist()}")
+        del dec
+        torch.cuda.empty_cache()
+
+    rn = _load_ref("rmsnorm")
+    sw = _load_ref("swiglu_fused")
+    res = {}
+    for b in OPS_CASE["batches"]:
+        x, w, resid, wg, wu, wd = (t.cuda() for t in ops_inputs(b))
+        out, rms = rn.forward(x, w, OPS_CASE["eps"])
+        r2 = resid.clone()
+        out_f, rms_f = rn.forward(x, w, OPS_CASE["eps"], r2)
+        torch.cuda.synchronize()
+        res[f"rms_out_{b}"] = out.view(torch.int16).cpu().numpy()
+        res[f"rms_rms_{b}"] = rms.cpu().numpy()
+        res[f"rmsf_out_{b}"] = out_f.view(torch.int16).cpu().numpy()
+        res[f"rmsf_res_{b}"] = r2.view(torch.int16).cpu().numpy()
+        res[f"rmsf_rms_{b}"] = rms_f.cpu().numpy()
+        if b in OPS_CASE["swiglu_batches"]:
+            t0 = time.time()
+            xs = out.view(b, 1, 1024)
+            y = sw.forward_down(xs, wg, wu, wd)
+            f, gc, uc = sw.forward(xs, wg, wu)
+            torch.cuda.synchronize()
+            res[f"swd_out_{b}"] = y.view(torch.int16).cpu().numpy()
+            res[f"swf_out_{b}"] = f.view(torch.int16).cpu().numpy()
+            print(f"swiglu B={b}: {time.time() - t0:.1f}s")
+    np.savez_compressed(os.path.join(args.out, "ref_ops.npz"), **res)
+    print("ops done")
+
+
+if __name__ == "__main__":
+    main()
