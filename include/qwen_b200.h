@@ -99,6 +99,18 @@ int qwen_b200_device_status(int device, uint64_t *detail);
  * nanoseconds (default 2e9).  Applies to later launches on all devices. */
 void qwen_b200_set_wait_timeout_ns(long long ns);
 
+/* Stage timeline for profiling (no upstream counterpart).  When a device
+ * buffer is registered, later decode launches write %globaltimer stamps into
+ * it: u64 [cta][step][layer 0..num_layers][32] for as many leading steps as
+ * fit in `bytes`.  Events per layer: stage A/B/C/D/E entry, after-wait and
+ * warp-0 end at 0..14; producer issue start / cumulative stall ns / issue end
+ * at 15..17; CTA-wide end of A/B/C/D/E at 18..22; cumulative ns consumer
+ * thread 0 waited for ring data at 23.  Row num_layers: final norm + lm_head
+ * entry, after-wait, end, argmax after-wait, end at 0..4.  Tracing adds one
+ * barrier per stage.  Pass NULL to turn it off.  The buffer must outlive the
+ * launches that use it. */
+void qwen_b200_set_trace(void *device_buffer, long long bytes);
+
 /* Failure-detection self test: launches one tiny kernel whose thread waits,
  * with the decode kernel's own bounded-wait routine, on a handoff word that
  * nothing writes.  Returns the status code that wait produced (the timeout

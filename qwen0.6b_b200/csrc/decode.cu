@@ -34,6 +34,7 @@
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -48,20 +49,39 @@ constexpr int QS = NQ * HD, KVS = NKV * HD, QKV_ROWS = QS + 2 * KVS;
 constexpr int VOCAB = 151936;
 constexpr float RMS_EPS = 1e-6f;
 
-constexpr int NCW = 16;               // consumer warps
+constexpr int NCW = 8;                // consumer warps
 constexpr int NCT = NCW * 32;         // consumer threads
 constexpr int NTHREADS = NCT + 32;    // + one producer warp
-constexpr int SLOT_BYTES = 12288;     // 6 rows of K=1024, 3 of 2048, 2 of 3072, 48 KV tokens
+// A ring piece carries up to PIECE_BYTES of payload: 6 weight rows of
+// K=1024, 3 of 2048, 2 of 3072, 48 KV-cache rows or 6 lm_head rows.  Weight
+// rows of the layer GEMVs are stored with a pitch of row_bytes + 16 and a
+// piece offset of 16 * (stage row index) mod 128, so that any 8 consecutive
+// stage rows start in 8 different 16-byte bank groups (conflict-free
+// ldmatrix); the slot keeps room for that padding.
+constexpr int PIECE_BYTES = 12288;
+constexpr int SLOT_BYTES = 12544;
 constexpr int NSLOTS = 16;
 constexpr int BATCH_MAX = 8;          // pieces per consumer batch (<= NSLOTS/2)
+// Bulk copies in flight per CTA (issued, not yet landed).  The ring may hold
+// up to NSLOTS landed pieces, but more bytes in flight than bandwidth x
+// latency only queue in the memory system and delay every other access on
+// the critical path (handoff words, norm weights).
+#ifndef QB200_INFLIGHT
+#define QB200_INFLIGHT 5
+#endif
+constexpr int INFLIGHT = QB200_INFLIGHT;
 constexpr int KV_ROW_BYTES = HD * 2;
-constexpr int KV_TOK_PER_PIECE = SLOT_BYTES / KV_ROW_BYTES;  // 48
+constexpr int KV_TOK_PER_PIECE = PIECE_BYTES / KV_ROW_BYTES;  // 48
 constexpr int SC_PAIRS = 3;                                  // K/V piece pairs per super-chunk
 constexpr int SC_TOK = SC_PAIRS * KV_TOK_PER_PIECE;          // 144
 constexpr int SPLIT_MIN_TOK = 64;
 constexpr int MAX_SPLITS = 32;
-constexpr int MIN_CTAS = 64, MAX_CTAS = 512;  // stage G gathers one CTA per consumer thread
-constexpr int MAX_OWN = 64;           // rows per CTA of o_proj/down/gate-up (C >= 64)
+// Splits the combine gathers in one round: C / NKV for a 148-SM B200.
+constexpr int MAX_SPLITS_B200 = 18;
+constexpr int MIN_CTAS = 128, MAX_CTAS = 256;  // stage G gathers one CTA per consumer thread
+constexpr int MAX_OWN = 64;           // rows per CTA of o_proj/down/gate-up
+constexpr int MAX_STAGE_ROWS = 48;    // GEMV rows per CTA and stage (C >= 128: QKV 32, gate+up 48)
+constexpr int MAX_TILES = MAX_STAGE_ROWS / 16;
 constexpr uint32_t BAR_ID = 1;
 
 enum Status : uint32_t {
@@ -112,7 +132,30 @@ struct DecodeArgs {
   uint32_t epoch_base;
   long long timeout_ns;
   Workspace ws;
+  // Optional stage timeline (null = off): [cta][step < trace_steps][layer 0..L][TR_N]
+  // %globaltimer stamps written by consumer thread 0 and the producer thread.
+  unsigned long long *trace;
+  int trace_steps;
 };
+
+enum TraceEv : int {
+  TR_A0 = 0, TR_A1, TR_A2, TR_B0, TR_B1, TR_B2, TR_C0, TR_C1, TR_C2, TR_D0, TR_D1, TR_D2,
+  TR_E0, TR_E1, TR_E2, TR_P_START, TR_P_STALL, TR_P_END,
+  TR_A3, TR_B3, TR_C3, TR_D3, TR_E3,   // CTA-wide stage end (after a consumer barrier)
+  TR_FW,                               // cumulative ns thread 0 waited on ring data
+  TR_N = 32
+};
+// Row l == num_layers holds the final stages: F entry / F after its wait /
+// F end / G after its wait / G end at events 0..4.
+
+__device__ __forceinline__ unsigned long long *trace_row(const DecodeArgs &a, int s, int l) {
+  if (a.trace == nullptr || s >= a.trace_steps) return nullptr;
+  return a.trace + ((static_cast<size_t>(blockIdx.x) * a.trace_steps + s) * (a.num_layers + 1) + l) * TR_N;
+}
+
+__device__ __forceinline__ void trace_mark(unsigned long long *row, int ev) {
+  if (row != nullptr && threadIdx.x == 0) row[ev] = globaltimer_ns();
+}
 
 struct __align__(128) Smem {
   uint8_t ring[NSLOTS][SLOT_BYTES];
@@ -125,11 +168,18 @@ struct __align__(128) Smem {
   float g_out[MAX_OWN], u_out[MAX_OWN], act_own[MAX_OWN];
   __half hid_own[MAX_OWN];
   __half qkv_raw[4 * HD];  // q head 2g, q head 2g+1, k head g, v head g
-  float q_rot[2][HD];
+  __half q_rot[2][HD];     // rotated q of the two heads (fp16, as upstream rounds it)
+  float wred[NCW][2];      // per-warp score max per head
+  float wsum[NCW];         // per-warp softmax sum
+  float pv[2][HD];         // attention output accumulators of the split
   __half k_fresh[HD];
   float sc[2][SC_TOK + 1];
   float att_m[2], att_l[2], att_alpha[2];
-  float accbuf[NCT];
+  float cmb_m[2][MAX_SPLITS], cmb_l[2][MAX_SPLITS];  // split (max, sum) per head
+  uint32_t rowaddr[MAX_TILES * 16];  // smem address of each GEMV stage row (padding rows -> row 0)
+  int rowinfo[MAX_TILES * 16];       // matrix row | kind << 24
+  float mred[NCW][MAX_TILES * 16];   // per-warp partial dot products
+  unsigned long long trace_fullwait;
   float wmax_val[NCW];
   int wmax_idx[NCW];
   float gmax_val[NCW];
@@ -142,6 +192,7 @@ static_assert(sizeof(Smem) + 1024 <= 232448, "decode kernel shared memory exceed
 
 // ------------------------------------------------------------------ waits
 struct WaitCtx {
+  unsigned long long *fullwait;  // tracing only: ns thread 0 spent waiting on ring data
   volatile uint32_t *abort;  // CTA-local
   unsigned long long *err;   // kernel-wide status word
   uint32_t tag;              // epoch base of this launch
@@ -154,18 +205,23 @@ __device__ __forceinline__ bool peer_failed(const WaitCtx &w) {
 }
 
 // Records (tag | code | where | cta) unless this launch already recorded one.
-__device__ __noinline__ void set_error(const WaitCtx &w, uint32_t code, uint32_t where) {
-  const unsigned long long mine = (static_cast<unsigned long long>(w.tag) << 32) |
+__device__ __noinline__ void set_error_word(unsigned long long *err, volatile uint32_t *abort_flag,
+                                            uint32_t tag, uint32_t code, uint32_t where) {
+  const unsigned long long mine = (static_cast<unsigned long long>(tag) << 32) |
                                   (static_cast<unsigned long long>(code & 0xff) << 24) |
                                   (static_cast<unsigned long long>(where & 0xff) << 16) |
                                   (blockIdx.x & 0xffff);
-  unsigned long long cur = atomicAdd(w.err, 0ull);
-  while (static_cast<uint32_t>(cur >> 32) != w.tag) {
-    const unsigned long long prev = atomicCAS(w.err, cur, mine);
+  unsigned long long cur = atomicAdd(err, 0ull);
+  while (static_cast<uint32_t>(cur >> 32) != tag) {
+    const unsigned long long prev = atomicCAS(err, cur, mine);
     if (prev == cur) break;
     cur = prev;
   }
-  *w.abort = 1;
+  *abort_flag = 1;
+}
+
+__device__ __forceinline__ void set_error(const WaitCtx &w, uint32_t code, uint32_t where) {
+  set_error_word(w.err, w.abort, w.tag, code, where);
 }
 
 // Slow path of a failed poll: returns false (and marks the CTA aborted) when
@@ -184,14 +240,22 @@ __device__ __forceinline__ bool wait_ok(const WaitCtx &w, uint64_t t0, uint32_t 
   return true;
 }
 
+__device__ __noinline__ bool wait_mbar_slow(WaitCtx w, uint64_t *bar, uint32_t parity,
+                                            uint32_t code, uint32_t where) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) {
+      if (w.fullwait != nullptr && threadIdx.x == 0) *w.fullwait += globaltimer_ns() - t0;
+      return true;
+    }
+    if ((it & 63) == 0 && !wait_ok(w, t0, code, where)) return false;
+  }
+}
+
 __device__ __forceinline__ bool wait_mbar(const WaitCtx &w, uint64_t *bar, uint32_t parity,
                                           uint32_t code, uint32_t where) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15) == 0 && !wait_ok(w, t0, code, where)) return false;
-  }
+  return wait_mbar_slow(w, bar, parity, code, where);
 }
 
 // Loads N handoff words (addresses from addr(i)) until all carry `epoch`;
@@ -209,6 +273,7 @@ __device__ __forceinline__ bool ll_gather(const WaitCtx &w, AddrFn addr, uint32_
   bool ok = true;
   if (!done) {
     const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
     for (uint32_t it = 1;; ++it) {
       done = true;
 #pragma unroll
@@ -219,7 +284,7 @@ __device__ __forceinline__ bool ll_gather(const WaitCtx &w, AddrFn addr, uint32_
         }
       }
       if (done) break;
-      if ((it & 7) == 0 && !wait_ok(w, t0, ST_TIMEOUT_LL, where)) {
+      if ((it & 31) == 0 && !wait_ok(w, t0, ST_TIMEOUT_LL, where)) {
         ok = false;
         break;
       }
@@ -231,9 +296,8 @@ __device__ __forceinline__ bool ll_gather(const WaitCtx &w, AddrFn addr, uint32_
 }
 
 // ------------------------------------------------------------ work layout
-__device__ __forceinline__ int part_lo(int n, int C, int c) {
-  return static_cast<int>((static_cast<long long>(n) * c) / C);
-}
+// n * c < 2^31 for every partition here (n <= 151936, c <= 512).
+__device__ __forceinline__ int part_lo(int n, int C, int c) { return (n * c) / C; }
 
 struct Piece {
   const char *src;
@@ -244,13 +308,15 @@ struct Piece {
 };
 
 __device__ __forceinline__ int npieces(int nrows, int row_bytes) {
-  const int rpp = SLOT_BYTES / row_bytes;
+  const int rpp = PIECE_BYTES / row_bytes;
   return (nrows + rpp - 1) / rpp;
 }
 
+__device__ __forceinline__ uint32_t row_pad(int stage_row) { return (16u * stage_row) & 127u; }
+
 __device__ __forceinline__ Piece seg_piece(const void *base, int row_bytes, int row0, int nrows,
                                            int i, int kind) {
-  const int rpp = SLOT_BYTES / row_bytes;
+  const int rpp = PIECE_BYTES / row_bytes;
   Piece P;
   const int r = i * rpp;
   P.row0 = row0 + r;
@@ -313,7 +379,7 @@ struct AttnGeom {
 __device__ __forceinline__ AttnGeom attn_geom(int p, int C, int c) {
   AttnGeom a;
   const int n_old = p;
-  const int smax = min(MAX_SPLITS, C / NKV);
+  const int smax = min(MAX_SPLITS_B200, C / NKV);
   a.S = n_old < SPLIT_MIN_TOK ? 1 : min(smax, (n_old + SPLIT_MIN_TOK - 1) / SPLIT_MIN_TOK);
   a.has = c < NKV * a.S;
   a.g = c / a.S;
@@ -337,6 +403,7 @@ __device__ __forceinline__ Piece kv_piece(const DecodeArgs &a, const AttnGeom &a
 
 __device__ __forceinline__ WaitCtx make_wait(const DecodeArgs &a, Smem &sm) {
   WaitCtx w;
+  w.fullwait = a.trace != nullptr ? &sm.trace_fullwait : nullptr;
   w.abort = &sm.abort;
   w.err = a.ws.err;
   w.tag = a.epoch_base;
@@ -345,27 +412,58 @@ __device__ __forceinline__ WaitCtx make_wait(const DecodeArgs &a, Smem &sm) {
 }
 
 // ------------------------------------------------------------- producer
-__device__ __noinline__ void producer(const DecodeArgs &a, Smem &sm) {
+// Issues ring piece n (one bulk copy, or one per padded weight row when
+// stage_row >= 0) after its slot was released and piece n-INFLIGHT landed.
+__device__ __noinline__ bool issue_piece(Smem &sm, WaitCtx w, uint32_t n, const char *src,
+                                         uint32_t bytes, int nrows, int stage_row, uint64_t pol,
+                                         unsigned long long *stall_ns) {
+  const int slot = n % NSLOTS;
+  const uint32_t round = n / NSLOTS;
+  if (round > 0 && !mbar_try_wait(&sm.empty[slot], (round - 1) & 1)) {
+    const uint64_t t0 = stall_ns ? globaltimer_ns() : 0;
+    if (!wait_mbar_slow(w, &sm.empty[slot], (round - 1) & 1, ST_TIMEOUT_EMPTY, W_PROD)) return false;
+    if (stall_ns) *stall_ns += globaltimer_ns() - t0;
+  }
+  if (n >= static_cast<uint32_t>(INFLIGHT)) {
+    // Piece n-INFLIGHT must have landed; its slot is reused only by piece
+    // n-INFLIGHT+NSLOTS > n, so this phase cannot have been overtaken.
+    const uint32_t m = n - INFLIGHT;
+    if (!wait_mbar(w, &sm.full[m % NSLOTS], (m / NSLOTS) & 1, ST_TIMEOUT_FULL, W_PROD)) return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) || (bytes & 15u) || bytes == 0 ||
+      bytes > static_cast<uint32_t>(PIECE_BYTES)) {
+    set_error(w, ST_MISALIGNED, W_PROD);
+    return false;
+  }
+  mbar_arrive_expect_tx(&sm.full[slot], bytes);
+  if (stage_row < 0) {
+    bulk_g2s(sm.ring[slot], src, bytes, &sm.full[slot], pol);
+  } else {
+    // Padded weight rows (see PIECE_BYTES): one copy per row.
+    const uint32_t rb = bytes / nrows;
+    uint8_t *dst = sm.ring[slot] + row_pad(stage_row);
+    for (int r = 0; r < nrows; ++r)
+      bulk_g2s(dst + r * (rb + 16), src + static_cast<size_t>(r) * rb, rb, &sm.full[slot], pol);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
   const int C = gridDim.x, c = blockIdx.x, L = a.num_layers;
   const WaitCtx w = make_wait(a, sm);
   const uint64_t pol = policy_evict_first();
   uint32_t n = 0;
   bool ok = true;
 
+  unsigned long long stall_ns = 0;
+  const bool tracing = a.trace != nullptr;
+  int stage_row = -1;  // >= 0: the GEMV stage row index of the next padded piece
   auto issue = [&](const Piece &P) -> bool {
-    const int slot = n % NSLOTS;
-    const uint32_t round = n / NSLOTS;
-    if (round > 0 && !wait_mbar(w, &sm.empty[slot], (round - 1) & 1, ST_TIMEOUT_EMPTY, W_PROD))
-      return false;
-    if ((reinterpret_cast<uintptr_t>(P.src) & 15u) || (P.bytes & 15u) || P.bytes == 0 ||
-        P.bytes > static_cast<uint32_t>(SLOT_BYTES)) {
-      set_error(w, ST_MISALIGNED, W_PROD);
-      return false;
-    }
-    mbar_arrive_expect_tx(&sm.full[slot], P.bytes);
-    bulk_g2s(sm.ring[slot], P.src, P.bytes, &sm.full[slot], pol);
+    const bool ok = issue_piece(sm, w, n, P.src, P.bytes, P.nrows, stage_row, pol,
+                                tracing ? &stall_ns : nullptr);
+    if (stage_row >= 0) stage_row += P.nrows;
     ++n;
-    return true;
+    return ok;
   };
 
   const QkvGeom qg = qkv_geom(C, c);
@@ -380,7 +478,14 @@ __device__ __noinline__ void producer(const DecodeArgs &a, Smem &sm) {
     const AttnGeom ag = attn_geom(p, C, c);
     for (int l = 0; l < L && ok; ++l) {
       const LayerPtrs lp = load_layer(a.layers, l);
+      unsigned long long *tr = trace_row(a, s, l);
+      if (tr) {
+        tr[TR_P_START] = globaltimer_ns();
+        tr[TR_P_STALL] = stall_ns;
+      }
+      stage_row = 0;
       for (int i = 0; i < qg.total && ok; ++i) ok = issue(qkv_piece(qg, lp, i));
+      stage_row = -1;
       if (ok && ag.has && ag.npairs > 0) {
         // Cached tokens written earlier in this launch must be visible to the
         // bulk-copy engine: wait for every KV write of the previous steps.
@@ -397,10 +502,15 @@ __device__ __noinline__ void producer(const DecodeArgs &a, Smem &sm) {
         }
         for (int i = 0; i < 2 * ag.npairs && ok; ++i) ok = issue(kv_piece(a, ag, l, i));
       }
+      stage_row = 0;
       for (int i = 0; i < o_np && ok; ++i) ok = issue(seg_piece(lp.w[6], 2 * QS, o_lo, o_n, i, 0));
+      stage_row = 0;
       for (int i = 0; i < 2 * gu_np && ok; ++i)
         ok = issue(seg_piece((i & 1) ? lp.w[9] : lp.w[8], 2 * H, gu_lo, gu_n, i >> 1, i & 1));
+      stage_row = 0;
       for (int i = 0; i < d_np && ok; ++i) ok = issue(seg_piece(lp.w[10], 2 * IM, o_lo, o_n, i, 0));
+      stage_row = -1;
+      if (tr) tr[TR_P_END] = globaltimer_ns();
     }
     for (int i = 0; i < lm_np && ok; ++i) ok = issue(seg_piece(a.lm_head, 2 * H, lm_lo, lm_n, i, 0));
   }
@@ -420,47 +530,132 @@ __device__ __noinline__ void producer(const DecodeArgs &a, Smem &sm) {
 }
 
 // -------------------------------------------------------------- consumers
-// Consumes `count` ring pieces of fp16 rows of length K (pieces from
-// get_piece(i)), batch by batch; row j of a batch goes to warp j % NCW.  The
-// activation vector x (fp16[K]) is read from shared memory.
-// epi(piece, matrix_row, dot) runs on every lane of the owning warp.
-template <int K, class GetPiece, class Epi>
-__device__ __forceinline__ bool gemv_pieces(Smem &sm, const WaitCtx &w, uint32_t &n, int count,
-                                            GetPiece get_piece, const __half *x, Epi epi,
-                                            uint32_t where) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  bool ok = true;
-  for (int b0 = 0; b0 < count; b0 += BATCH_MAX) {
-    const int nb = min(BATCH_MAX, count - b0);
-    int j0 = 0;
-    for (int i = 0; i < nb; ++i) {
-      const Piece P = get_piece(b0 + i);
-      const uint32_t pn = n + i;
-      const int slot = pn % NSLOTS;
-      int r = (warp - j0) % NCW;
-      if (r < 0) r += NCW;
-      if (r < P.nrows) ok &= wait_mbar(w, &sm.full[slot], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, where);
-      for (; r < P.nrows; r += NCW) {
-        const __half *row = reinterpret_cast<const __half *>(sm.ring[slot] + r * (K * 2));
-        float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < K / 256; jj += 2) {
-          const int o0 = lane * 8 + 256 * jj;
-          acc0 = dot8_hh(*reinterpret_cast<const uint4 *>(row + o0),
-                         *reinterpret_cast<const uint4 *>(x + o0), acc0);
-          acc1 = dot8_hh(*reinterpret_cast<const uint4 *>(row + o0 + 256),
-                         *reinterpret_cast<const uint4 *>(x + o0 + 256), acc1);
-        }
-        epi(P, P.row0 + r, warp_sum(acc0 + acc1));
-      }
-      j0 += P.nrows;
+// Row table of a GEMV stage whose `count` pieces start at ring piece n:
+// thread j (< MAX_TILES*16) records the smem address of stage row j, and its
+// matrix row and kind.  Rows past the end point at row 0 (their results are
+// ignored).  Each thread writes and later reads only its own entry, so no
+// barrier is needed between one stage's epilogue and the next table.
+template <int K, class GetPiece>
+__device__ __forceinline__ int prep_rows(Smem &sm, uint32_t n, int count, GetPiece get_piece) {
+  constexpr int PITCH = 2 * K + 16;
+  const int j = threadIdx.x;
+  int total = 0;
+  uint32_t addr0 = 0, my_addr = 0;
+  int my_info = 0;
+  bool found = false;
+  for (int i = 0; i < count; ++i) {
+    const Piece P = get_piece(i);
+    const uint32_t base = smem_u32(sm.ring[(n + i) % NSLOTS]) + row_pad(total);
+    if (i == 0) addr0 = base;
+    if (!found && j < total + P.nrows) {
+      my_addr = base + (j - total) * PITCH;
+      my_info = (P.row0 + (j - total)) | (P.kind << 24);
+      found = true;
     }
-    __syncwarp();
-    if (lane == 0)
-      for (int i = 0; i < nb; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
-    n += nb;
+    total += P.nrows;
   }
-  return ok;
+  if (j < MAX_TILES * 16) {
+    sm.rowaddr[j] = found ? my_addr : addr0;
+    sm.rowinfo[j] = found ? my_info : -1;
+  }
+  return total;
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2,
+                                        uint32_t &a3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Batch-1 GEMV of a stage on the tensor cores: y[j] = W[j,:] . x for the
+// `total` rows of the row table (pieces n .. n+count-1, all landed before
+// use).  The vector x (fp16[K], shared memory) is column 0 of the B operand;
+// rows are the A operand (ldmatrix from the padded ring rows); warp w takes
+// K/16/NCW of the K steps for all row tiles, and the per-warp partial sums
+// are added in a fixed order, so results are deterministic.  The tensor
+// cores here cut instruction count (the stage is latency- and HBM-bound);
+// fp16 products are exact and accumulate in fp32.
+// epi(kind, matrix_row, dot) runs on thread j for stage row j < total.
+template <int K, class Epi>
+__device__ __forceinline__ void gemv_mma(Smem &sm, uint32_t &n, int count, int total,
+                                         const __half *x, Epi epi) {
+  constexpr int KS_W = K / 16 / NCW;
+  static_assert(KS_W % 2 == 0, "two accumulator chains");
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tiles = (total + 15) >> 4;
+  // Two independent accumulator chains per tile (even / odd K steps).
+  float d[MAX_TILES][4], e[MAX_TILES][4];
+#pragma unroll
+  for (int t = 0; t < MAX_TILES; ++t)
+    d[t][0] = d[t][1] = d[t][2] = d[t][3] = e[t][0] = e[t][1] = e[t][2] = e[t][3] = 0.f;
+  const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
+  const uint32_t lcol = (lane >> 4) * 16;  // bytes
+  uint32_t rbase[MAX_TILES];
+#pragma unroll
+  for (int t = 0; t < MAX_TILES; ++t) rbase[t] = sm.rowaddr[t * 16 + lrow] + lcol;
+#pragma unroll 2
+  for (int q = 0; q < KS_W; q += 2) {
+    const int k0 = (warp * KS_W + q) * 16;
+    uint32_t b0 = 0, b1 = 0, c0 = 0, c1 = 0;
+    if (lane < 4) {
+      b0 = *reinterpret_cast<const uint32_t *>(x + k0 + 2 * lane);
+      b1 = *reinterpret_cast<const uint32_t *>(x + k0 + 8 + 2 * lane);
+      c0 = *reinterpret_cast<const uint32_t *>(x + k0 + 16 + 2 * lane);
+      c1 = *reinterpret_cast<const uint32_t *>(x + k0 + 24 + 2 * lane);
+    }
+#pragma unroll
+    for (int t = 0; t < MAX_TILES; ++t) {
+      if (t < tiles) {
+        uint32_t a0, a1, a2, a3, f0, f1, f2, f3;
+        ldsm_x4(rbase[t] + k0 * 2, a0, a1, a2, a3);
+        ldsm_x4(rbase[t] + k0 * 2 + 32, f0, f1, f2, f3);
+        mma16816(d[t], a0, a1, a2, a3, b0, b1);
+        mma16816(e[t], f0, f1, f2, f3, c0, c1);
+      }
+    }
+  }
+  if ((lane & 3) == 0) {
+#pragma unroll
+    for (int t = 0; t < MAX_TILES; ++t) {
+      if (t < tiles) {
+        sm.mred[warp][t * 16 + (lane >> 2)] = d[t][0] + e[t][0];
+        sm.mred[warp][t * 16 + (lane >> 2) + 8] = d[t][2] + e[t][2];
+      }
+    }
+  }
+  named_bar_sync(BAR_ID, NCT);
+  if (lane == 0)
+    for (int i = 0; i < count; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
+  n += count;
+  if (tid < total) {
+    float dot = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < NCW; ++ww) dot += sm.mred[ww][tid];
+    const int info = sm.rowinfo[tid];
+    epi(info >> 24, info & 0xffffff, dot);
+  }
+}
+
+// Waits until the `count` (<= 32) ring pieces from n on have landed: lane i
+// of warp 0 waits on piece i, so the waits overlap.  Called before a stage's
+// first barrier, which then orders the pieces' shared memory before every
+// consumer thread's reads.
+__device__ __forceinline__ bool wait_pieces(Smem &sm, const WaitCtx &w, uint32_t n, int count,
+                                            uint32_t where) {
+  const int tid = threadIdx.x;
+  if (tid >= count) return true;
+  const uint32_t pn = n + tid;
+  return wait_mbar(w, &sm.full[pn % NSLOTS], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, where);
 }
 
 __device__ __forceinline__ __half silu_half(float g) {
@@ -474,216 +669,21 @@ __device__ __forceinline__ __half silu_half(float g) {
   return __hmul(x, r);
 }
 
-// Stage B.  Returns true when the CTA must abort (uniform across consumers).
-__device__ __noinline__ bool attention(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                          const AttnGeom &ag, int l, int p, uint32_t ep, const LayerPtrs &lp,
-                          bool &fail) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = ag.g;
-  {
-    const int word = tid < 256 ? (256 * g + tid)
-                               : (tid < 384 ? (QS + 128 * g + tid - 256) : (QS + KVS + 128 * g + tid - 384));
-    uint32_t u[1];
-    fail |= !ll_gather<1>(w, [&](int) { return a.ws.qkv + word; }, ep, u, W_B);
-    sm.qkv_raw[tid] = u2h(u[0]);
-    if (tid < 2) {
-      sm.att_m[tid] = -INFINITY;
-      sm.att_l[tid] = 0.f;
-    }
-  }
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
+// ======================================================================
+// Consumer warps (NCW = 8, all stages inlined into the kernel: no calls, no
+// stack, kernel parameters read straight from the parameter space).
+// ======================================================================
 
-  // q/k RMSNorm (eps 1e-6) + rotate-half RoPE, megakernel.cu:345-434.
-  if (warp < 2 || (ag.last && warp == 2)) {
-    const __half *src = sm.qkv_raw + warp * HD;
-    const __half *nw = warp < 2 ? lp.w[4] : lp.w[5];
-    const __half *cosp = a.cos_t + static_cast<size_t>(p) * HD;
-    const __half *sinp = a.sin_t + static_cast<size_t>(p) * HD;
-    float xv[4], ss = 0.f;
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      xv[it] = __half2float(src[lane + 32 * it]);
-      ss = fmaf(xv[it], xv[it], ss);
-    }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
-    float vals[4];
-#pragma unroll
-    for (int it = 0; it < 4; ++it)
-      vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), __half2float(__ldg(nw + lane + 32 * it)));
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int i = lane + 32 * it;
-      const int ri = it < 2 ? i : i - HD / 2;
-      const float cs = __half2float(__ldg(cosp + ri)), sn = __half2float(__ldg(sinp + ri));
-      const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], cs), __fmul_rn(vals[it + 2], sn))
-                             : __fadd_rn(__fmul_rn(vals[it - 2], sn), __fmul_rn(vals[it], cs));
-      const __half hr = __float2half(r);
-      if (warp < 2) sm.q_rot[warp][i] = __half2float(hr);
-      else sm.k_fresh[i] = hr;
-    }
-  }
-  named_bar_sync(BAR_ID, NCT);
+struct St {
+  uint32_t n;  // ring pieces consumed so far
+  bool fail;   // this thread saw a failed wait
+};
 
-  if (ag.last) {
-    // New token's K (rotated) and V (raw) into the cache at position p.
-    const size_t off = ((static_cast<size_t>(l) * NKV + g) * a.max_seq + p) * HD;
-    if (tid < HD) a.k_cache[off + tid] = sm.k_fresh[tid];
-    else if (tid < 2 * HD) a.v_cache[off + tid - HD] = sm.qkv_raw[3 * HD + tid - HD];
-    if (tid < 2 * HD) {
-      fence_proxy_async_global();
-      __threadfence();
-    }
-    named_bar_sync(BAR_ID, NCT);
-    if (tid == 0) red_release_add_u32(a.ws.kv_ready, 1);
-  }
-
-  const int pair = tid & 255, hh = pair >> 7, dd = pair & 127, par = tid >> 8;
-  float acc = 0.f;
-  const int total_old = ag.t1 - ag.t0;
-  for (int sc = 0; sc < ag.nsc; ++sc) {
-    const int pair0 = sc * SC_PAIRS;
-    const int npair = max(0, min(SC_PAIRS, ag.npairs - pair0));
-    const int n_old = max(0, min(SC_TOK, total_old - pair0 * KV_TOK_PER_PIECE));
-    const bool fresh = ag.last && (sc == ag.nsc - 1);
-    const int ntok = n_old + (fresh ? 1 : 0);
-    // Scores: one warp per token, lanes over 4 dims each.
-    for (int tt = warp; tt < ntok; tt += NCW) {
-      const __half *krow;
-      if (tt < n_old) {
-        const uint32_t pn = n + 2 * (tt / KV_TOK_PER_PIECE);
-        fail |= !wait_mbar(w, &sm.full[pn % NSLOTS], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, W_B);
-        krow = reinterpret_cast<const __half *>(sm.ring[pn % NSLOTS] + (tt % KV_TOK_PER_PIECE) * KV_ROW_BYTES);
-      } else {
-        krow = sm.k_fresh;
-      }
-      const uint2 kv = *reinterpret_cast<const uint2 *>(krow + 4 * lane);
-      const float2 k01 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.x));
-      const float2 k23 = __half22float2(*reinterpret_cast<const __half2 *>(&kv.y));
-      const float4 q0 = *reinterpret_cast<const float4 *>(&sm.q_rot[0][4 * lane]);
-      const float4 q1 = *reinterpret_cast<const float4 *>(&sm.q_rot[1][4 * lane]);
-      float d0 = q0.x * k01.x;
-      d0 = fmaf(q0.y, k01.y, d0);
-      d0 = fmaf(q0.z, k23.x, d0);
-      d0 = fmaf(q0.w, k23.y, d0);
-      float d1 = q1.x * k01.x;
-      d1 = fmaf(q1.y, k01.y, d1);
-      d1 = fmaf(q1.z, k23.x, d1);
-      d1 = fmaf(q1.w, k23.y, d1);
-      d0 = warp_sum(d0);
-      d1 = warp_sum(d1);
-      if (lane == 0) {
-        sm.sc[0][tt] = d0 * a.attn_scale;
-        sm.sc[1][tt] = d1 * a.attn_scale;
-      }
-    }
-    named_bar_sync(BAR_ID, NCT);
-    // Online softmax update per head (expf as upstream, :490-494).
-    if (warp < 2 && ntok > 0) {
-      float mx = -INFINITY;
-      for (int tt = lane; tt < ntok; tt += 32) mx = fmaxf(mx, sm.sc[warp][tt]);
-      mx = warp_max(mx);
-      const float m_old = sm.att_m[warp];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int tt = lane; tt < ntok; tt += 32) {
-        const float pr = expf(sm.sc[warp][tt] - m_new);
-        sm.sc[warp][tt] = pr;
-        sum += pr;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
-        sm.att_alpha[warp] = alpha;
-        sm.att_l[warp] = sm.att_l[warp] * alpha + sum;
-        sm.att_m[warp] = m_new;
-      }
-    } else if (warp < 2 && lane == 0) {
-      sm.att_alpha[warp] = 1.f;
-    }
-    named_bar_sync(BAR_ID, NCT);
-    // P.V: thread (head hh, dim dd) over tokens of parity `par`.
-    acc *= sm.att_alpha[hh];
-    for (int tt = par; tt < ntok; tt += 2) {
-      __half vv;
-      if (tt < n_old) {
-        const uint32_t pn = n + 2 * (tt / KV_TOK_PER_PIECE) + 1;
-        if ((tt % KV_TOK_PER_PIECE) < 2)
-          fail |= !wait_mbar(w, &sm.full[pn % NSLOTS], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, W_B);
-        vv = reinterpret_cast<const __half *>(sm.ring[pn % NSLOTS] +
-                                              (tt % KV_TOK_PER_PIECE) * KV_ROW_BYTES)[dd];
-      } else {
-        vv = sm.qkv_raw[3 * HD + dd];
-      }
-      acc = fmaf(sm.sc[hh][tt], __half2float(vv), acc);
-    }
-    named_bar_sync(BAR_ID, NCT);
-    if (lane == 0)
-      for (int i = 0; i < 2 * npair; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
-    n += 2 * npair;
-  }
-
-  sm.accbuf[tid] = acc;
-  named_bar_sync(BAR_ID, NCT);
-  if (tid < 256) {
-    const int h = tid >> 7, d = tid & 127;
-    float val = sm.accbuf[tid] + sm.accbuf[tid + 256];
-    float m = sm.att_m[h], lsum = sm.att_l[h];
-    bool write_out = false;
-    if (ag.S > 1 && ag.j != 0) {
-      uint64_t *pp = a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + ag.j) * 2 + h) * (HD + 2);
-      ll_store(pp + d, __float_as_uint(val), ep);
-      if (d < 2) ll_store(pp + HD + d, __float_as_uint(d == 0 ? m : lsum), ep);
-    } else if (ag.S > 1) {
-      // Combiner (split 0): merge the other splits' (m, l, acc), 8 at a time.
-      for (int j0 = 1; j0 < ag.S; j0 += 4) {
-        uint32_t u[12];
-        const int jn = min(4, ag.S - j0);
-        fail |= !ll_gather<12>(
-            w,
-            [&](int i) {
-              const int jj = j0 + min(i / 3, jn - 1);
-              const uint64_t *pp =
-                  a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + h) * (HD + 2);
-              const int k = i % 3;
-              return pp + (k == 0 ? d : HD + k - 1);
-            },
-            ep, u, W_B);
-        for (int q = 0; q < jn; ++q) {
-          const float aj = __uint_as_float(u[3 * q]), mj = __uint_as_float(u[3 * q + 1]),
-                      lj = __uint_as_float(u[3 * q + 2]);
-          if (mj == -INFINITY) continue;
-          if (m == -INFINITY) {
-            m = mj;
-            lsum = lj;
-            val = aj;
-            continue;
-          }
-          const float mn = fmaxf(m, mj);
-          const float f0 = expf(m - mn), f1 = expf(mj - mn);
-          val = val * f0 + aj * f1;
-          lsum = lsum * f0 + lj * f1;
-          m = mn;
-        }
-      }
-      write_out = true;
-    } else {
-      write_out = true;
-    }
-    if (write_out) {
-      const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
-      const __half o = __float2half(val * inv);
-      const int col = (2 * g + h) * HD + d;
-      a.attn_out[col] = o;
-      const uint32_t other = __shfl_down_sync(0xffffffffu, h2u(o), 1);
-      if ((d & 1) == 0) ll_store(a.ws.attn + col / 2, h2u(o) | (other << 16), ep);
-    }
-  }
-  return false;
+__device__ __forceinline__ const __half *layer_ptr(const LDGLayerWeight *t, int l, int idx) {
+  return reinterpret_cast<const __half *>(
+      __ldg(reinterpret_cast<const unsigned long long *>(t + l) + idx));
 }
 
-// Per-CTA row ranges of the stage GEMVs (same split for o_proj and down, so
-// a CTA owns the same hidden rows in stages C and E).
 struct Rows {
   int lo, n;
 };
@@ -694,123 +694,454 @@ __device__ __forceinline__ Rows rows_of(int total, int C, int c) {
   return r;
 }
 
-__device__ __forceinline__ const __half *layer_ptr(const LDGLayerWeight *t, int l, int idx) {
-  return reinterpret_cast<const __half *>(
-      __ldg(reinterpret_cast<const unsigned long long *>(t + l) + idx));
+// Sum of a per-thread float over the consumer threads: warp reduce, one
+// named barrier that also ORs the abort predicate (returned in *abort), then
+// every thread adds the NCW warp sums in the same order.
+__device__ __forceinline__ float block_sum(Smem &sm, float v, bool pred, bool *abort) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = v;
+  *abort = named_bar_or(BAR_ID, NCT, pred);
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCW; ++i) t += sm.red[i];
+  return t;
 }
 
-// Stage A: input RMSNorm (megakernel.cu:806-847) + fused QKV GEMV (:242-291).
-// Returns true when the CTA must abort (uniform across consumer threads).
-__device__ __noinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                                     bool &fail, int l, int token, uint32_t ep) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int C = gridDim.x, c = blockIdx.x;
-  float h0, h1;
+// ---------------------------------------------------------------- stage A
+// Input RMSNorm (megakernel.cu:806-847) + fused QKV GEMV (:242-291).
+__device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        int l, int token, uint32_t ep, unsigned long long *tr) {
+  const int tid = threadIdx.x, C = gridDim.x, c = blockIdx.x;
+  trace_mark(tr, TR_A0);
+  const QkvGeom qg = qkv_geom(C, c);
+  const LayerPtrs lp{};  // consumers only need row ranges, not addresses
+  const int total = prep_rows<H>(sm, st.n, qg.total, [&](int i) { return qkv_piece(qg, lp, i); });
+  const __half *nw = layer_ptr(a.layers, l, 0);
+  float wv[4], h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(nw + tid + NCT * i));
+  st.fail |= !wait_pieces(sm, w, st.n, qg.total, W_A);
   if (l == 0) {
     const __half *emb = a.embed + static_cast<size_t>(token) * H;
-    h0 = __half2float(__ldg(emb + tid));
-    h1 = __half2float(__ldg(emb + tid + NCT));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __half2float(__ldg(emb + tid + NCT * i));
     const Rows o = rows_of(H, C, c);
     if (tid < o.n) sm.hid_own[tid] = __ldg(emb + o.lo + tid);
   } else {
-    uint32_t u[2];
-    fail |= !ll_gather<2>(w, [&](int i) { return a.ws.hidden + tid + i * NCT; }, ep - 1, u, W_A);
-    h0 = __half2float(u2h(u[0]));
-    h1 = __half2float(u2h(u[1]));
-  }
-  const float ss = warp_sum(fmaf(h0, h0, h1 * h1));
-  if (lane == 0) sm.red[warp] = ss;
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
-  {
-    float tot = 0.f;
+    uint32_t u[4];
+    st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.hidden + tid + NCT * i; }, ep - 1, u, W_A);
 #pragma unroll
-    for (int i = 0; i < NCW; ++i) tot += sm.red[i];
-    const float inv = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
-    const __half *nw = layer_ptr(a.layers, l, 0);
-    sm.xa[tid] = __float2half(h0 * (inv * __half2float(__ldg(nw + tid))));
-    sm.xa[tid + NCT] = __float2half(h1 * (inv * __half2float(__ldg(nw + tid + NCT))));
+    for (int i = 0; i < 4; ++i) h[i] = __half2float(u2h(u[i]));
   }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(h[i], h[i], ss);
+  bool abort;
+  const float tot = block_sum(sm, ss, st.fail || sm.abort, &abort);
+  if (abort) return true;
+  trace_mark(tr, TR_A1);
+  const float inv = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sm.xa[tid + NCT * i] = __float2half(h[i] * (inv * wv[i]));
   named_bar_sync(BAR_ID, NCT);
-  const QkvGeom qg = qkv_geom(C, c);
-  const LayerPtrs lp{};  // consumers only need row ranges, not addresses
-  fail |= !gemv_pieces<H>(
-      sm, w, n, qg.total, [&](int i) { return qkv_piece(qg, lp, i); }, sm.xa,
-      [&](const Piece &P, int row, float dot) {
-        if (lane == 0) {
-          const __half hv = __float2half(dot);
-          const int vrow = (P.kind == 0 ? 0 : (P.kind == 1 ? QS : QS + KVS)) + row;
-          ll_store(a.ws.qkv + vrow, h2u(hv), ep);
-          __half *dst = P.kind == 0 ? a.q : (P.kind == 1 ? a.k : a.v);
-          dst[row] = hv;
-        }
-      },
-      W_A);
+  gemv_mma<H>(
+      sm, st.n, qg.total, total, sm.xa,
+      [&](int kind, int row, float dot) {
+        const __half hv = __float2half(dot);
+        const int vrow = (kind == 0 ? 0 : (kind == 1 ? QS : QS + KVS)) + row;
+        ll_store(a.ws.qkv + vrow, h2u(hv), ep);
+        __half *dst = kind == 0 ? a.q : (kind == 1 ? a.k : a.v);
+        dst[row] = hv;
+      });
+  trace_mark(tr, TR_A2);
   return false;
 }
 
-// Stage C: o_proj GEMV + fp32 residual (megakernel.cu:585-610, :868-872).
-__device__ __noinline__ bool stage_c(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                                     bool &fail, uint32_t ep) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  {
-    uint32_t u[2];
-    fail |= !ll_gather<2>(w, [&](int i) { return a.ws.attn + tid + i * NCT; }, ep, u, W_C);
-    reinterpret_cast<uint32_t *>(sm.xb)[tid] = u[0];
-    reinterpret_cast<uint32_t *>(sm.xb)[tid + NCT] = u[1];
-  }
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
-  const Rows o = rows_of(H, gridDim.x, blockIdx.x);
-  fail |= !gemv_pieces<QS>(
-      sm, w, n, npieces(o.n, 2 * QS), [&](int i) { return seg_piece(nullptr, 2 * QS, o.lo, o.n, i, 0); },
-      sm.xb,
-      [&](const Piece &, int row, float dot) {
-        if (lane == 0) {
-          const float resid = __half2float(sm.hid_own[row - o.lo]);
-          const float act = dot + resid;
-          ll_store(a.ws.act + row, __float_as_uint(act), ep);
-          a.act[row] = act;
-          a.res[row] = resid;
-          sm.act_own[row - o.lo] = act;
-        }
-      },
-      W_C);
-  return false;
-}
-
-// Stage D: post-attention RMSNorm from fp32 act (megakernel.cu:614-638) +
-// gate/up GEMV + half SiLU * up (:640-675).
-__device__ __noinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                                     bool &fail, int l, uint32_t ep) {
+// ---------------------------------------------------------------- stage B
+// q/k RMSNorm + RoPE, KV-cache write, split-KV GQA attention over the cache
+// and the combine of the splits (megakernel.cu:308-553).
+__device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        const AttnGeom &ag, int l, int p, uint32_t ep,
+                                        unsigned long long *tr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float h0, h1;
+  const int g = ag.g;
+  trace_mark(tr, TR_B0);
+  // Loads that do not depend on this layer's activations go first.
+  const bool rope_warp = warp < 2 || (ag.last && warp == 2);
+  float nwv[4] = {0.f, 0.f, 0.f, 0.f}, csv[4] = {0.f, 0.f, 0.f, 0.f}, snv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (rope_warp) {
+    const __half *nw = layer_ptr(a.layers, l, warp < 2 ? 4 : 5);
+    const __half *cosp = a.cos_t + static_cast<size_t>(p) * HD;
+    const __half *sinp = a.sin_t + static_cast<size_t>(p) * HD;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int i = lane + 32 * it;
+      const int ri = it < 2 ? i : i - HD / 2;
+      nwv[it] = __half2float(__ldg(nw + i));
+      csv[it] = __half2float(__ldg(cosp + ri));
+      snv[it] = __half2float(__ldg(sinp + ri));
+    }
+  }
   {
     uint32_t u[2];
-    fail |= !ll_gather<2>(w, [&](int i) { return a.ws.act + tid + i * NCT; }, ep, u, W_D);
-    h0 = __uint_as_float(u[0]);
-    h1 = __uint_as_float(u[1]);
-    const float ss = warp_sum(fmaf(h0, h0, h1 * h1));
-    if (lane == 0) sm.red[warp] = ss;
+    st.fail |= !ll_gather<2>(
+        w,
+        [&](int i) {
+          const int t2 = tid + NCT * i;
+          const int word = t2 < 256 ? (256 * g + t2)
+                                    : (t2 < 384 ? (QS + 128 * g + t2 - 256) : (QS + KVS + 128 * g + t2 - 384));
+          return a.ws.qkv + word;
+        },
+        ep, u, W_B);
+    sm.qkv_raw[tid] = u2h(u[0]);
+    sm.qkv_raw[tid + NCT] = u2h(u[1]);
+    if (tid < 2) {
+      sm.att_m[tid] = -INFINITY;
+      sm.att_l[tid] = 0.f;
+    }
   }
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
-  {
-    float tot = 0.f;
+  if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+  trace_mark(tr, TR_B1);
+
+  // q/k RMSNorm (eps 1e-6) + rotate-half RoPE, megakernel.cu:345-434.
+  if (rope_warp) {
+    const __half *src = sm.qkv_raw + warp * HD;
+    float xv[4], ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < NCW; ++i) tot += sm.red[i];
-    const float rstd = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
-    const __half *nw = layer_ptr(a.layers, l, 7);
-    sm.xa[tid] = __float2half(__half2float(__float2half(h0)) * rstd * __half2float(__ldg(nw + tid)));
-    sm.xa[tid + NCT] =
-        __float2half(__half2float(__float2half(h1)) * rstd * __half2float(__ldg(nw + tid + NCT)));
+    for (int it = 0; it < 4; ++it) {
+      xv[it] = __half2float(src[lane + 32 * it]);
+      ss = fmaf(xv[it], xv[it], ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+    float vals[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), nwv[it]);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int i = lane + 32 * it;
+      const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], csv[it]), __fmul_rn(vals[it + 2], snv[it]))
+                             : __fadd_rn(__fmul_rn(vals[it - 2], snv[it]), __fmul_rn(vals[it], csv[it]));
+      const __half hr = __float2half(r);
+      if (warp < 2) sm.q_rot[warp][i] = hr;
+      else sm.k_fresh[i] = hr;
+    }
+    if (warp == 2 && ag.last) {
+      // New token's K (rotated) and V (raw) into the cache at position p,
+      // 8 bytes per lane; later steps of this launch read the entry with bulk
+      // copies, hence the proxy fence and the release count.
+      __syncwarp();
+      const size_t off = ((static_cast<size_t>(l) * NKV + g) * a.max_seq + p) * HD + 4 * lane;
+      *reinterpret_cast<uint2 *>(a.k_cache + off) = *reinterpret_cast<const uint2 *>(sm.k_fresh + 4 * lane);
+      *reinterpret_cast<uint2 *>(a.v_cache + off) =
+          *reinterpret_cast<const uint2 *>(sm.qkv_raw + 3 * HD + 4 * lane);
+      if (a.num_steps > 1) {
+        // Publication: __syncwarp orders the lanes' stores before lane 0's
+        // release; the reader acquires the count and issues a proxy fence
+        // before its bulk copy (see the producer).
+        __syncwarp();
+        if (lane == 0) red_release_add_u32(a.ws.kv_ready, 1);
+      }
+    }
   }
   named_bar_sync(BAR_ID, NCT);
+
+  // A fragments of q (m16n8k16, rows 0/1 = the two q heads, other rows 0):
+  // lanes 0..7 hold q[lane/4][16kk + 2(lane%4) + {0,1}] and the +8 columns.
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    qa[kk][0] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][16 * kk + 2 * (lane & 3)]) : 0u;
+    qa[kk][1] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][16 * kk + 8 + 2 * (lane & 3)]) : 0u;
+  }
+  const int hh = tid >> 7;                       // head of this thread (softmax, P.V)
+  const int dpair = tid & 63, par = (tid >> 6) & 1;  // P.V: dims 2*dpair..+1, token parity
+  float acc0 = 0.f, acc1 = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  const int total_old = ag.t1 - ag.t0;
+  uint32_t n = st.n;
+#pragma unroll 1
+  for (int sc = 0; sc < ag.nsc; ++sc) {
+    const int pair0 = sc * SC_PAIRS;
+    const int npair = max(0, min(SC_PAIRS, ag.npairs - pair0));
+    const int n_old = max(0, min(SC_TOK, total_old - pair0 * KV_TOK_PER_PIECE));
+    const bool fresh = ag.last && (sc == ag.nsc - 1);
+    const int ntok = n_old + (fresh ? 1 : 0);
+    // This super-chunk's K/V pieces: warp 0 waits, the barrier publishes.
+    st.fail |= !wait_pieces(sm, w, n, 2 * npair, W_B);
+    named_bar_sync(BAR_ID, NCT);
+    // Scores S[h][t] = q_h . k_t on the tensor cores (fp16 inputs, exact
+    // products, fp32 accumulation), 8 tokens per tile, tiles over warps.
+    float wmax = -INFINITY;  // lanes 0..3: head 0, lanes 4..7: head 1
+    const int ntile = (ntok + 7) >> 3;
+#pragma unroll 1
+    for (int tile = warp; tile < ntile; tile += NCW) {
+      const int tok = tile * 8 + (lane >> 2);
+      const __half *krow = sm.k_fresh;
+      if (tok < n_old) {
+        const uint32_t pn = n + 2 * (tok / KV_TOK_PER_PIECE);
+        krow = reinterpret_cast<const __half *>(sm.ring[pn % NSLOTS] + (tok % KV_TOK_PER_PIECE) * KV_ROW_BYTES);
+      }
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 2 * (lane & 3));
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 8 + 2 * (lane & 3));
+        mma16816(d, qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+      }
+      if (lane < 8) {
+        const int t0 = tile * 8 + 2 * (lane & 3);
+        const float s0 = d[0] * a.attn_scale, s1 = d[1] * a.attn_scale;
+        if (t0 < ntok) {
+          sm.sc[lane >> 2][t0] = s0;
+          wmax = fmaxf(wmax, s0);
+        }
+        if (t0 + 1 < ntok) {
+          sm.sc[lane >> 2][t0 + 1] = s1;
+          wmax = fmaxf(wmax, s1);
+        }
+      }
+    }
+    wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, 1));
+    wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, 2));
+    if (lane == 0 || lane == 4) sm.wred[warp][lane >> 2] = wmax;
+    named_bar_sync(BAR_ID, NCT);
+    // Softmax (expf as upstream, megakernel.cu:490-494): every thread of head
+    // hh derives the same running max, turns its tokens' scores into weights.
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NCW; ++i) cmax = fmaxf(cmax, sm.wred[i][hh]);
+    const float m_new = fmaxf(m_run, cmax);
+    float psum = 0.f;
+    if (ntok > 0) {
+      for (int tt = tid & 127; tt < ntok; tt += 128) {
+        const float pr = expf(sm.sc[hh][tt] - m_new);
+        sm.sc[hh][tt] = pr;
+        psum += pr;
+      }
+    }
+    psum = warp_sum(psum);
+    if (lane == 0) sm.wsum[warp] = psum;
+    named_bar_sync(BAR_ID, NCT);
+    {
+      float tsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < NCW / 2; ++i) tsum += sm.wsum[hh * (NCW / 2) + i];
+      const float alpha = ntok == 0 ? 1.f : (m_run == -INFINITY ? 0.f : expf(m_run - m_new));
+      if (ntok > 0) {
+        l_run = l_run * alpha + tsum;
+        m_run = m_new;
+      }
+      acc0 *= alpha;
+      acc1 *= alpha;
+    }
+    // P.V: dims 2*dpair, 2*dpair+1 of head hh over the tokens of parity par.
+    {
+      float b0 = 0.f, b1 = 0.f;
+      const float *pr = sm.sc[hh];
+#pragma unroll 1
+      for (int t0 = 0; t0 < n_old; t0 += KV_TOK_PER_PIECE) {
+        const uint32_t pn = n + 2 * (t0 / KV_TOK_PER_PIECE) + 1;
+        const __half2 *vcol = reinterpret_cast<const __half2 *>(sm.ring[pn % NSLOTS]) + dpair;
+        const int cnt = min(KV_TOK_PER_PIECE, n_old - t0);
+        int tt = par;
+#pragma unroll 2
+        for (; tt + 2 < cnt; tt += 4) {
+          const float2 v0 = __half22float2(vcol[tt * (HD / 2)]);
+          const float2 v1 = __half22float2(vcol[(tt + 2) * (HD / 2)]);
+          const float p0 = pr[t0 + tt], p1 = pr[t0 + tt + 2];
+          acc0 = fmaf(p0, v0.x, acc0);
+          acc1 = fmaf(p0, v0.y, acc1);
+          b0 = fmaf(p1, v1.x, b0);
+          b1 = fmaf(p1, v1.y, b1);
+        }
+        for (; tt < cnt; tt += 2) {
+          const float2 v0 = __half22float2(vcol[tt * (HD / 2)]);
+          acc0 = fmaf(pr[t0 + tt], v0.x, acc0);
+          acc1 = fmaf(pr[t0 + tt], v0.y, acc1);
+        }
+      }
+      if (fresh && par == (n_old & 1)) {
+        const float2 v0 = __half22float2(reinterpret_cast<const __half2 *>(sm.qkv_raw + 3 * HD)[dpair]);
+        acc0 = fmaf(pr[n_old], v0.x, acc0);
+        acc1 = fmaf(pr[n_old], v0.y, acc1);
+      }
+      acc0 += b0;
+      acc1 += b1;
+    }
+    named_bar_sync(BAR_ID, NCT);
+    if (lane == 0)
+      for (int i = 0; i < 2 * npair; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
+    n += 2 * npair;
+  }
+  st.n = n;
+  // Add the two token parities; thread (h, d) then holds output dim d of head h.
+  if (par == 1) {
+    sm.pv[hh][2 * dpair] = acc0;
+    sm.pv[hh][2 * dpair + 1] = acc1;
+  }
+  named_bar_sync(BAR_ID, NCT);
+  if (par == 0) {
+    sm.pv[hh][2 * dpair] += acc0;
+    sm.pv[hh][2 * dpair + 1] += acc1;
+    if (dpair == 0) {
+      sm.att_m[hh] = m_run;
+      sm.att_l[hh] = l_run;
+    }
+  }
+  named_bar_sync(BAR_ID, NCT);
+  const int dd = tid & 127;
+  const float acc = sm.pv[hh][dd];
+  {
+    const int h = hh, d = dd;
+    float val = acc;
+    float m = sm.att_m[h], lsum = sm.att_l[h];
+    if (ag.S > 1 && ag.j != 0) {
+      uint64_t *pp = a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + ag.j) * 2 + h) * (HD + 2);
+      ll_store(pp + d, __float_as_uint(val), ep);
+      if (d < 2) ll_store(pp + HD + d, __float_as_uint(d == 0 ? m : lsum), ep);
+    }
+    if (ag.S > 1 && ag.j == 0) {
+      // Combiner (split 0).  Phase 1: thread 2*jj + h (jj >= 1) fetches split
+      // jj's (m, l) for head h into shared memory.
+      if (tid < 2 * ag.S && tid >= 2) {
+        const int jj = tid >> 1, hq = tid & 1;
+        const uint64_t *pp = a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + hq) * (HD + 2);
+        uint32_t u[2];
+        st.fail |= !ll_gather<2>(w, [&](int i) { return pp + HD + i; }, ep, u, W_B);
+        sm.cmb_m[hq][jj] = __uint_as_float(u[0]);
+        sm.cmb_l[hq][jj] = __uint_as_float(u[1]);
+      }
+      if (tid < 2) {
+        sm.cmb_m[tid][0] = sm.att_m[tid];
+        sm.cmb_l[tid][0] = sm.att_l[tid];
+      }
+    }
+    if (ag.S > 1) named_bar_sync(BAR_ID, NCT);
+    bool write_out = ag.S == 1 || ag.j == 0;
+    if (ag.S > 1 && ag.j == 0) {
+      // Phase 2: global max, then acc = sum_j acc_j * exp(m_j - M) and
+      // l = sum_j l_j * exp(m_j - M).
+      float M = -INFINITY;
+#pragma unroll 1
+      for (int jj = 0; jj < ag.S; ++jj) M = fmaxf(M, sm.cmb_m[h][jj]);
+      float A = 0.f, Ls = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll 1
+        for (int jj = 0; jj < ag.S; ++jj) {
+          const float mj = sm.cmb_m[h][jj];
+          const float f = mj == -INFINITY ? 0.f : expf(mj - M);
+          Ls += sm.cmb_l[h][jj] * f;
+          if (jj == 0) A += val * f;
+        }
+        // The other splits' acc words, 9 splits per round (loads of a round
+        // are issued together).
+#pragma unroll 1
+        for (int j0 = 1; j0 < ag.S; j0 += 9) {
+          uint32_t u[9];
+          const int jn = min(9, ag.S - j0);
+          st.fail |= !ll_gather<9>(
+              w,
+              [&](int i) {
+                const int jj = j0 + min(i, jn - 1);
+                return a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + h) * (HD + 2) + d;
+              },
+              ep, u, W_B);
+#pragma unroll
+          for (int q = 0; q < 9; ++q) {
+            if (q < jn) {
+              const float mj = sm.cmb_m[h][j0 + q];
+              if (mj != -INFINITY) A = fmaf(__uint_as_float(u[q]), expf(mj - M), A);
+            }
+          }
+        }
+      }
+      val = A;
+      lsum = Ls;
+    }
+    if (write_out) {
+      const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+      const __half o = __float2half(val * inv);
+      const int col = (2 * g + h) * HD + d;
+      const uint32_t other = __shfl_down_sync(0xffffffffu, h2u(o), 1);
+      if ((d & 1) == 0) ll_store(a.ws.attn + col / 2, h2u(o) | (other << 16), ep);
+      a.attn_out[col] = o;
+    }
+  }
+  trace_mark(tr, TR_B2);
+  return false;
+}
+
+// ---------------------------------------------------------------- stage C
+// o_proj GEMV + fp32 residual (megakernel.cu:585-610, :868-872).
+__device__ __forceinline__ bool stage_c(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        uint32_t ep, unsigned long long *tr) {
+  const int tid = threadIdx.x;
+  trace_mark(tr, TR_C0);
+  const Rows o = rows_of(H, gridDim.x, blockIdx.x);
+  const int np = npieces(o.n, 2 * QS);
+  const int total =
+      prep_rows<QS>(sm, st.n, np, [&](int i) { return seg_piece(nullptr, 2 * QS, o.lo, o.n, i, 0); });
+  st.fail |= !wait_pieces(sm, w, st.n, np, W_C);
+  {
+    uint32_t u[4];
+    st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.attn + tid + NCT * i; }, ep, u, W_C);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<uint32_t *>(sm.xb)[tid + NCT * i] = u[i];
+  }
+  if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+  trace_mark(tr, TR_C1);
+  gemv_mma<QS>(
+      sm, st.n, np, total, sm.xb,
+      [&](int, int row, float dot) {
+        const float resid = __half2float(sm.hid_own[row - o.lo]);
+        const float act = dot + resid;
+        ll_store(a.ws.act + row, __float_as_uint(act), ep);
+        sm.act_own[row - o.lo] = act;
+        a.act[row] = act;
+        a.res[row] = resid;
+      });
+  trace_mark(tr, TR_C2);
+  return false;
+}
+
+// ---------------------------------------------------------------- stage D
+// Post-attention RMSNorm from fp32 act (megakernel.cu:614-638) + gate/up GEMV
+// + half SiLU * up (:640-675).
+__device__ __forceinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        int l, uint32_t ep, unsigned long long *tr) {
+  const int tid = threadIdx.x;
+  trace_mark(tr, TR_D0);
   const Rows gu = rows_of(IM, gridDim.x, blockIdx.x);
-  fail |= !gemv_pieces<H>(
-      sm, w, n, 2 * npieces(gu.n, 2 * H),
-      [&](int i) { return seg_piece(nullptr, 2 * H, gu.lo, gu.n, i >> 1, i & 1); }, sm.xa,
-      [&](const Piece &P, int row, float dot) {
-        if (lane == 0) (P.kind == 0 ? sm.g_out : sm.u_out)[row - gu.lo] = dot;
-      },
-      W_D);
+  const int np = 2 * npieces(gu.n, 2 * H);
+  const int total = prep_rows<H>(
+      sm, st.n, np, [&](int i) { return seg_piece(nullptr, 2 * H, gu.lo, gu.n, i >> 1, i & 1); });
+  const __half *nw = layer_ptr(a.layers, l, 7);
+  float wv[4], h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(nw + tid + NCT * i));
+  st.fail |= !wait_pieces(sm, w, st.n, np, W_D);
+  {
+    uint32_t u[4];
+    st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.act + tid + NCT * i; }, ep, u, W_D);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __uint_as_float(u[i]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(h[i], h[i], ss);
+  bool abort;
+  const float tot = block_sum(sm, ss, st.fail || sm.abort, &abort);
+  if (abort) return true;
+  trace_mark(tr, TR_D1);
+  const float rstd = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    sm.xa[tid + NCT * i] = __float2half(__half2float(__float2half(h[i])) * rstd * wv[i]);
+  named_bar_sync(BAR_ID, NCT);
+  gemv_mma<H>(sm, st.n, np, total, sm.xa, [&](int kind, int row, float dot) {
+    (kind == 0 ? sm.g_out : sm.u_out)[row - gu.lo] = dot;
+  });
   named_bar_sync(BAR_ID, NCT);
   if (tid < gu.n) {
     const float act = __half2float(silu_half(sm.g_out[tid])) * sm.u_out[tid];
@@ -818,61 +1149,72 @@ __device__ __noinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const WaitCt
     ll_store(a.ws.inter + row, h2u(__float2half(act)), ep);
     a.inter[row] = act;
   }
+  trace_mark(tr, TR_D2);
   return false;
 }
 
-// Stage E: down GEMV on half(mlp_inter) + residual, rounded to fp16
-// (megakernel.cu:679-707).
-__device__ __noinline__ bool stage_e(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                                     bool &fail, uint32_t ep) {
-  const int tid = threadIdx.x, lane = tid & 31;
+// ---------------------------------------------------------------- stage E
+// Down GEMV on half(mlp_inter) + residual, rounded to fp16 (megakernel.cu:679-707).
+__device__ __forceinline__ bool stage_e(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        uint32_t ep, unsigned long long *tr) {
+  const int tid = threadIdx.x;
+  trace_mark(tr, TR_E0);
+  const Rows o = rows_of(H, gridDim.x, blockIdx.x);
+  const int np = npieces(o.n, 2 * IM);
+  const int total =
+      prep_rows<IM>(sm, st.n, np, [&](int i) { return seg_piece(nullptr, 2 * IM, o.lo, o.n, i, 0); });
+  st.fail |= !wait_pieces(sm, w, st.n, np, W_E);
   {
     uint32_t u[IM / NCT];
-    fail |= !ll_gather<IM / NCT>(w, [&](int i) { return a.ws.inter + tid + i * NCT; }, ep, u, W_E);
+    st.fail |= !ll_gather<IM / NCT>(w, [&](int i) { return a.ws.inter + tid + NCT * i; }, ep, u, W_E);
 #pragma unroll
-    for (int i = 0; i < IM / NCT; ++i) sm.xb[tid + i * NCT] = u2h(u[i]);
+    for (int i = 0; i < IM / NCT; ++i) sm.xb[tid + NCT * i] = u2h(u[i]);
   }
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
-  const Rows o = rows_of(H, gridDim.x, blockIdx.x);
-  fail |= !gemv_pieces<IM>(
-      sm, w, n, npieces(o.n, 2 * IM), [&](int i) { return seg_piece(nullptr, 2 * IM, o.lo, o.n, i, 0); },
-      sm.xb,
-      [&](const Piece &, int row, float dot) {
-        if (lane == 0) {
-          const __half hv = __float2half(dot + sm.act_own[row - o.lo]);
-          ll_store(a.ws.hidden + row, h2u(hv), ep);
-          a.hidden[row] = hv;
-          sm.hid_own[row - o.lo] = hv;
-        }
-      },
-      W_E);
+  if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+  trace_mark(tr, TR_E1);
+  gemv_mma<IM>(
+      sm, st.n, np, total, sm.xb,
+      [&](int, int row, float dot) {
+        const __half hv = __float2half(dot + sm.act_own[row - o.lo]);
+        ll_store(a.ws.hidden + row, h2u(hv), ep);
+        sm.hid_own[row - o.lo] = hv;
+        a.hidden[row] = hv;
+      });
+  trace_mark(tr, TR_E2);
   return false;
 }
 
-// Stage F: final RMSNorm to fp32 (megakernel.cu:890-919), tied lm_head GEMV
-// and this CTA's argmax (:1001-1109; lowest index among equal maxima).
-__device__ __noinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCtx &w, uint32_t &n,
-                                     bool &fail, int s, uint32_t ep_last) {
+// ---------------------------------------------------------------- stage F
+// Final RMSNorm to fp32 (megakernel.cu:890-919), tied lm_head GEMV and this
+// CTA's argmax (:1001-1109; lowest index among equal maxima).
+__device__ __forceinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        int s, uint32_t ep_last, unsigned long long *tr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
+  trace_mark(tr, 0);
+  if (tr != nullptr && tid == 0) tr[5] = static_cast<unsigned long long>(clock64());
   {
-    uint32_t u[2];
-    fail |= !ll_gather<2>(w, [&](int i) { return a.ws.hidden + tid + i * NCT; }, ep_last, u, W_F);
-    const float f0 = __half2float(u2h(u[0])), f1 = __half2float(u2h(u[1]));
-    const float ssum = warp_sum(fmaf(f0, f0, f1 * f1));
-    if (lane == 0) sm.red[warp] = ssum;
-    if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
-    float tot = 0.f;
+    float wv[4], h[4];
 #pragma unroll
-    for (int i = 0; i < NCW; ++i) tot += sm.red[i];
+    for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(a.final_norm + tid + NCT * i));
+    uint32_t u[4];
+    st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.hidden + tid + NCT * i; }, ep_last, u, W_F);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[i] = __half2float(u2h(u[i]));
+      ss = fmaf(h[i], h[i], ss);
+    }
+    bool abort;
+    const float tot = block_sum(sm, ss, st.fail || sm.abort, &abort);
+    if (abort) return true;
+    trace_mark(tr, 1);
     const float inv = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
-    const float n0 = f0 * inv * __half2float(__ldg(a.final_norm + tid));
-    const float n1 = f1 * inv * __half2float(__ldg(a.final_norm + tid + NCT));
-    sm.xf[tid] = n0;
-    sm.xf[tid + NCT] = n1;
-    if (c == 0) {
-      a.norm_out[tid] = n0;
-      a.norm_out[tid + NCT] = n1;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float nv = h[i] * inv * wv[i];
+      sm.xf[tid + NCT * i] = nv;
+      if (c == 0) a.norm_out[tid + NCT * i] = nv;
     }
   }
   named_bar_sync(BAR_ID, NCT);
@@ -886,6 +1228,7 @@ __device__ __noinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCt
   }
   float best = -INFINITY;
   int bidx = 0x7fffffff;
+  uint32_t n = st.n;
   for (int b0 = 0; b0 < lm_np; b0 += BATCH_MAX) {
     const int nb = min(BATCH_MAX, lm_np - b0);
     int j0 = 0;
@@ -895,7 +1238,7 @@ __device__ __noinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCt
       const int slot = pn % NSLOTS;
       int r = (warp - j0) % NCW;
       if (r < 0) r += NCW;
-      if (r < P.nrows) fail |= !wait_mbar(w, &sm.full[slot], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, W_F);
+      if (r < P.nrows) st.fail |= !wait_mbar(w, &sm.full[slot], (pn / NSLOTS) & 1, ST_TIMEOUT_FULL, W_F);
       for (; r < P.nrows; r += NCW) {
         const __half *row = reinterpret_cast<const __half *>(sm.ring[slot] + r * (2 * H));
         float acc0 = 0.f, acc1 = 0.f;
@@ -920,6 +1263,7 @@ __device__ __noinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCt
       for (int i = 0; i < nb; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
     n += nb;
   }
+  st.n = n;
   if (lane == 0) {
     sm.wmax_val[warp] = best;
     sm.wmax_idx[warp] = bidx;
@@ -942,13 +1286,15 @@ __device__ __noinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const WaitCt
     a.bmax_vals[c] = bv;
     a.bmax_idxs[c] = bi;
   }
+  trace_mark(tr, 2);
   return false;
 }
 
-// Stage G: global argmax over the per-CTA results (megakernel.cu:1114-1144),
-// lowest index among equal maxima.  Sets *token_out (uniform).
-__device__ __noinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCtx &w, bool &fail,
-                                     int s, int *token_out) {
+// ---------------------------------------------------------------- stage G
+// Global argmax over the per-CTA results (megakernel.cu:1114-1144), lowest
+// index among equal maxima.  Sets *token (uniform).
+__device__ __forceinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
+                                        int s, int *token, unsigned long long *tr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = gridDim.x;
   float v = -INFINITY;
@@ -956,7 +1302,7 @@ __device__ __noinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCt
   if (tid < C) {
     uint32_t u[2];
     const uint32_t eps_ = a.epoch_base + static_cast<uint32_t>(s);
-    fail |= !ll_gather<2>(w, [&](int i) { return a.ws.amax + i * MAX_CTAS + tid; }, eps_, u, W_G);
+    st.fail |= !ll_gather<2>(w, [&](int i) { return a.ws.amax + i * MAX_CTAS + tid; }, eps_, u, W_G);
     v = __uint_as_float(u[0]);
     id = static_cast<int>(u[1]);
   }
@@ -973,7 +1319,8 @@ __device__ __noinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCt
     sm.gmax_val[warp] = v;
     sm.gmax_idx[warp] = id;
   }
-  if (named_bar_or(BAR_ID, NCT, fail || sm.abort)) return true;
+  if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+  trace_mark(tr, 3);
   float bv = sm.gmax_val[0];
   int bi = sm.gmax_idx[0];
   for (int i = 1; i < NCW; ++i) {
@@ -985,33 +1332,53 @@ __device__ __noinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCt
     }
   }
   if (blockIdx.x == 0 && tid == 0) a.out_tokens[s] = bi;
-  *token_out = (bi >= 0 && bi < VOCAB) ? bi : 0;
+  *token = (bi >= 0 && bi < VOCAB) ? bi : 0;
+  trace_mark(tr, 4);
+  if (tr != nullptr && tid == 0) tr[6] = static_cast<unsigned long long>(clock64());
   return false;
 }
 
-__device__ void consumer(const DecodeArgs &a, Smem &sm) {
+// CTA-wide end of a stage (tracing only: one extra barrier per stage).
+__device__ __forceinline__ void trace_end(Smem &sm, unsigned long long *tr, int ev) {
+  if (tr != nullptr) {
+    named_bar_sync(BAR_ID, NCT);
+    trace_mark(tr, ev);
+    if (threadIdx.x == 0) tr[TR_FW] = sm.trace_fullwait;
+  }
+}
+
+__device__ __forceinline__ void consumer(const DecodeArgs &a, Smem &sm) {
   const int C = gridDim.x, c = blockIdx.x, L = a.num_layers;
   const WaitCtx w = make_wait(a, sm);
-  uint32_t n = 0;
+  St st;
+  st.n = 0;
+  st.fail = false;
   int token = a.first_token;
-  bool fail = false;
   int s = 0;
   for (s = 0; s < a.num_steps; ++s) {
     const int p = a.start_pos + s;
+    const AttnGeom ag = attn_geom(p, C, c);
     for (int l = 0; l < L; ++l) {
       const uint32_t ep = a.epoch_base + static_cast<uint32_t>(s * L + l);
-      if (stage_a(sm, a, w, n, fail, l, token, ep)) goto out;
-      const AttnGeom ag = attn_geom(p, C, c);
+      unsigned long long *tr = trace_row(a, s, l);
+      if (stage_a(sm, a, w, st, l, token, ep, tr)) goto out;
+      trace_end(sm, tr, TR_A3);
       if (ag.has) {
-        const LayerPtrs lp = load_layer(a.layers, l);
-        if (attention(sm, a, w, n, ag, l, p, ep, lp, fail)) goto out;
+        if (stage_b(sm, a, w, st, ag, l, p, ep, tr)) goto out;
+        trace_end(sm, tr, TR_B3);
       }
-      if (stage_c(sm, a, w, n, fail, ep)) goto out;
-      if (stage_d(sm, a, w, n, fail, l, ep)) goto out;
-      if (stage_e(sm, a, w, n, fail, ep)) goto out;
+      if (stage_c(sm, a, w, st, ep, tr)) goto out;
+      trace_end(sm, tr, TR_C3);
+      if (stage_d(sm, a, w, st, l, ep, tr)) goto out;
+      trace_end(sm, tr, TR_D3);
+      if (stage_e(sm, a, w, st, ep, tr)) goto out;
+      trace_end(sm, tr, TR_E3);
     }
-    if (stage_f(sm, a, w, n, fail, s, a.epoch_base + static_cast<uint32_t>(s * L + L - 1))) goto out;
-    if (stage_g(sm, a, w, fail, s, &token)) goto out;
+    {
+      unsigned long long *trf = trace_row(a, s, L);
+      if (stage_f(sm, a, w, st, s, a.epoch_base + static_cast<uint32_t>(s * L + L - 1), trf)) goto out;
+      if (stage_g(sm, a, w, st, s, &token, trf)) goto out;
+    }
   }
   return;
 out:
@@ -1019,9 +1386,11 @@ out:
     for (int s2 = s; s2 < a.num_steps; ++s2) a.out_tokens[s2] = -1;
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(smem_raw);
+  // 128-byte aligned base: the padded row layout relies on slot bases that
+  // are multiples of 128 bytes.
+  Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int i = 0; i < NSLOTS; ++i) {
@@ -1029,6 +1398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const DecodeArgs a)
       mbar_init(&sm.empty[i], NCW);
     }
     sm.abort = 0;
+    sm.trace_fullwait = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -1047,6 +1417,7 @@ __global__ void selftest_wait_kernel(uint64_t *word, unsigned long long *err, lo
   __syncthreads();
   if (threadIdx.x != 0) return;
   WaitCtx w;
+  w.fullwait = nullptr;
   w.abort = &abort_flag;
   w.err = err;
   w.tag = tag;
@@ -1075,6 +1446,8 @@ struct DevState {
 std::mutex g_mu;
 DevState g_dev[64];
 long long g_timeout_ns = 2000000000LL;
+unsigned long long *g_trace = nullptr;
+long long g_trace_bytes = 0;
 thread_local int t_err = 0;
 thread_local char t_msg[512] = {0};
 
@@ -1145,6 +1518,10 @@ DevState *get_dev(int *dev_out) {
   d.mem = mem;
   d.ll_bytes = ll_bytes;
   d.num_sms = sms;
+  if (const char *env = getenv("QB200_CTAS")) {
+    const int want = atoi(env);
+    if (want >= MIN_CTAS && want <= sms) d.num_sms = want;
+  }
   d.epoch = 1;
   d.ready = true;
   return &d;
@@ -1192,6 +1569,16 @@ int launch_decode(DecodeArgs &a, cudaStream_t st) {
   d->last_tag = a.epoch_base;
   a.timeout_ns = g_timeout_ns;
   a.ws = d->ws;
+  a.trace = nullptr;
+  a.trace_steps = 0;
+  if (g_trace != nullptr) {
+    const long long per_step = static_cast<long long>(d->num_sms) * (a.num_layers + 1) * TR_N * 8;
+    const long long steps = per_step > 0 ? g_trace_bytes / per_step : 0;
+    if (steps > 0) {
+      a.trace = g_trace;
+      a.trace_steps = static_cast<int>(steps < a.num_steps ? steps : a.num_steps);
+    }
+  }
   if (a.num_steps > 1) cudaMemsetAsync(d->ws.kv_ready, 0, sizeof(uint32_t), st);
   void *args[] = {&a};
   cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void *>(decode_kernel),
@@ -1215,6 +1602,11 @@ int qwen_b200_last_error(char *msg, int msg_len) {
 }
 
 void qwen_b200_set_wait_timeout_ns(long long ns) { g_timeout_ns = ns > 0 ? ns : 2000000000LL; }
+
+void qwen_b200_set_trace(void *device_buffer, long long bytes) {
+  g_trace = static_cast<unsigned long long *>(device_buffer);
+  g_trace_bytes = device_buffer ? bytes : 0;
+}
 
 int qwen_b200_device_status(int device, uint64_t *detail) {
   if (device < 0 || device >= 64) return -1;

@@ -89,14 +89,17 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // aligned relaxed accesses at gpu scope are single-copy atomic, so a reader
 // that sees the expected epoch also sees the payload written with it, and
 // the read never hits a stale L1 line.
+// No "memory" clobber: these relaxed accesses order nothing else, and a
+// clobber would force every value the compiler holds from memory (kernel
+// parameters included) to be reloaded after each handoff access.
 __device__ __forceinline__ void ll_store(uint64_t *p, uint32_t payload, uint32_t epoch) {
   uint64_t v = (static_cast<uint64_t>(epoch) << 32) | payload;
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v));
 }
 
 __device__ __forceinline__ uint64_t ll_load(const uint64_t *p) {
   uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
   return v;
 }
 
