@@ -182,6 +182,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
+                    help="prefilled tokens before the timed steps (workload: 1920)")
+    ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -213,18 +216,19 @@ def main() -> None:
     w_gpu["lm_head_weight"] = w_gpu["embed_weight"]
     dec = Decoder(weights=w_gpu, verbose=False)
 
+    plen, gen = args.prompt_len, args.gen
     g = torch.Generator().manual_seed(SEED + 1)
-    prompt = torch.randint(0, 151936, (PROMPT_LEN,), generator=g).tolist()
+    prompt = torch.randint(0, 151936, (plen,), generator=g).tolist()
     first = None
-    for t in prompt:                       # untimed prefill, positions 0..1919
+    for t in prompt:                       # untimed prefill, positions 0..plen-1
         first = dec.step(t)
-    assert dec.position == PROMPT_LEN
+    assert dec.position == plen
 
     stream = torch.cuda.current_stream(dev)
 
     def one_step():
-        dec._position = PROMPT_LEN
-        return dec.generate_nosync(first, GEN)
+        dec._position = plen
+        return dec.generate_nosync(first, gen)
 
     for _ in range(args.warmup):
         one_step()
@@ -261,8 +265,8 @@ def main() -> None:
     for i in range(args.steps):
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        dec._position = PROMPT_LEN
-        toks = dec.generate_nosync(first, GEN).cpu()
+        dec._position = plen
+        toks = dec.generate_nosync(first, gen).cpu()
         e2e_ms.append(1000.0 * (time.perf_counter() - t0))
         assert toks.tolist() == ref_tokens
 
@@ -273,21 +277,22 @@ def main() -> None:
     else:
         e2e_total = sum(e2e_ms)
 
-    value = world * GEN * args.steps / (total_ms / 1000.0)
-    e2e_value = world * GEN * args.steps / (e2e_total / 1000.0)
+    value = world * gen * args.steps / (total_ms / 1000.0)
+    e2e_value = world * gen * args.steps / (e2e_total / 1000.0)
     avg_launch_s = statistics.mean(launch_ms) / 1000.0
-    alg = algorithmic_bytes(PROMPT_LEN, GEN)
+    alg = algorithmic_bytes(plen, gen)
     peaks = measured_peaks()
     achieved = alg / avg_launch_s / 1e9
-    traffic = profile_traffic()
+    traffic = profile_traffic() if (plen, gen) == (PROMPT_LEN, GEN) else None
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded random-init weights, uniform-random token ids)",
-        "config": {"workload": "config 2: batch-1 greedy decode, 1920-token seeded prompt "
-                               "prefilled (untimed), 128 steps at positions 1920..2047 per step",
-                   "batch": 1, "prompt_len": PROMPT_LEN, "gen_steps": GEN,
+        "config": {"workload": f"config 2: batch-1 greedy decode, {plen}-token seeded prompt "
+                               f"prefilled (untimed), {gen} steps at positions {plen}..{plen + gen - 1}"
+                               " per step",
+                   "batch": 1, "prompt_len": plen, "gen_steps": gen,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (1.19 GB of weights read per token); no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
@@ -295,7 +300,7 @@ def main() -> None:
                      "peak_src": peaks["src"], "traffic": traffic,
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg_launch_s * 1000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
-                "d2h_bytes_per_step": 4 * GEN},
+                "d2h_bytes_per_step": 4 * gen},
         "gpu_launches": args.steps,
         "clocks": clk,
     }

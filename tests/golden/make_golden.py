@@ -181,8 +181,13 @@ def run_ops(args):
         if b in OPS_CASE["swiglu_batches"]:
             t0 = time.time()
             xs = out.view(b, 1, 1024)
-            y = sw.forward_down(xs, wg, wu, wd)
-            f, gc, uc = sw.forward(xs, wg, wu)
+            # The upstream binding's optional biases default to an undefined
+            # tensor, which this torch version does not convert from None;
+            # zero biases give the same fp16 accumulation start value.
+            zg = torch.zeros(3072, dtype=torch.float16, device=xs.device)
+            zd = torch.zeros(1024, dtype=torch.float16, device=xs.device)
+            y = sw.forward_down(xs, wg, wu, wd, zg, zg, zd)
+            f, gc, uc = sw.forward(xs, wg, wu, zg, zg)
             torch.cuda.synchronize()
             res[f"swd_out_{b}"] = y.view(torch.int16).cpu().numpy()
             res[f"swf_out_{b}"] = f.view(torch.int16).cpu().numpy()
