@@ -85,6 +85,40 @@ void launch_ldg_generate_nosync(
     void *block_max_vals, void *block_max_idxs, int *output_log, int num_layers,
     int start_position, int max_seq_len, float attn_scale, void *stream);
 
+/*
+ * launch_ldg_generate_nosync_static_ws has no counterpart in the reference.
+ * Same parameters and results as launch_ldg_generate_nosync, but it never
+ * allocates device memory: the kernel's scratch (stage handoff words, attention
+ * split partials, per-CTA argmax, status word) is a fixed 618,752-byte array
+ * compiled into this library, one copy per device.  It is for callers that
+ * cannot have a library allocate behind their back: a server that hands all of
+ * HBM to its own pool up front (a cudaMalloc at call time would fail or
+ * fragment it), or a latency-critical loop where cudaMalloc's implicit device
+ * synchronisation is not acceptable.
+ * - The first call on each device does a one-time set-up with that device
+ *   current: it looks the array up (cudaGetSymbolAddress, which may load this
+ *   library's kernels on the device) and clears it with a synchronous memset.
+ *   Make that first call before any stream capture.
+ * - The array is sized for at most 256 SMs and 32 attention splits per KV
+ *   head; it does not grow with sequence length, steps or layers.  A device
+ *   that would need more is rejected with an error; so are the arguments
+ *   launch_ldg_generate_nosync rejects.
+ * - Calls on one device share the array: calls that overlap in time (other
+ *   streams, other host threads without ordering) race and corrupt each other.
+ *   Order them, e.g. on one stream.
+ * - Device-side failures show as -1 tokens in output_log;
+ *   qwen_b200_device_status() reports on the allocating launchers only.
+ * Returns 0 when the launch was issued, else the qwen_b200_last_error() code.
+ */
+int launch_ldg_generate_nosync_static_ws(
+    int first_token_id, int num_steps, const void *embed_weight,
+    const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table, void *k_cache,
+    void *v_cache, void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+    void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate, void *g_normalized,
+    void *block_max_vals, void *block_max_idxs, int *output_log, int num_layers,
+    int start_position, int max_seq_len, float attn_scale, void *stream);
+
 /* Error reporting (no upstream counterpart: the upstream megakernel launchers
  * return void and check no CUDA errors, qwen_ops.cpp:34-165).
  * qwen_b200_last_error: 0 if the calling thread's last launcher call was

@@ -1426,7 +1426,19 @@ __global__ void selftest_wait_kernel(uint64_t *word, unsigned long long *err, lo
   ll_gather<1>(w, [&](int) { return word; }, 0xfffffff0u, u, W_SELFTEST);
 }
 
+// Handoff words of one decode launch (the Workspace layout below), plus 32
+// words for the KV-ready counter and the status word.
+constexpr size_t WS_LL_WORDS = H + QKV_ROWS + QS / 2 + H + IM +
+                               static_cast<size_t>(NKV) * MAX_SPLITS * 2 * (HD + 2) + 2 * MAX_CTAS;
+constexpr size_t WS_TAIL_WORDS = 32;
+
 }  // namespace qb200
+
+// Fixed workspace of launch_ldg_generate_nosync_static_ws: 618,752 bytes per
+// device, enough for up to MAX_CTAS (256) CTAs and MAX_SPLITS (32) attention
+// splits per KV head.  Loaded with the module, so that entry point never
+// allocates.  One copy per device, shared by every call on that device.
+static __device__ __align__(256) uint64_t g_static_ws[qb200::WS_LL_WORDS + qb200::WS_TAIL_WORDS];
 
 // ====================================================================== host
 using namespace qb200;
@@ -1462,49 +1474,48 @@ int fail_msg(int code, const char *fmt, ...) {
 
 size_t smem_bytes() { return sizeof(Smem) + 1024; }
 
-DevState *get_dev(int *dev_out) {
+int current_device(int *dev_out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     fail_msg(2, "cudaGetDevice failed");
-    return nullptr;
+    return 0;
   }
   *dev_out = dev;
-  DevState &d = g_dev[dev];
-  if (d.ready) return &d;
+  return 1;
+}
+
+// Checks that `dev` can run the decode kernel and sets its shared-memory
+// attribute.  Returns the device's SM count, or 0 with the error recorded.
+int probe_device(int dev) {
   int sms = 0, coop = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
   if (!coop) {
     fail_msg(3, "device %d does not support cooperative launch", dev);
-    return nullptr;
+    return 0;
   }
   if (sms < MIN_CTAS || sms > MAX_CTAS) {
     fail_msg(3, "device %d has %d SMs; this kernel needs %d..%d", dev, sms, MIN_CTAS, MAX_CTAS);
-    return nullptr;
+    return 0;
   }
   cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem_bytes()));
   if (e != cudaSuccess) {
     fail_msg(4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    return nullptr;
+    return 0;
   }
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, NTHREADS, smem_bytes());
   if (per_sm < 1) {
     fail_msg(4, "decode kernel does not fit on an SM (%zu B shared memory)", smem_bytes());
-    return nullptr;
+    return 0;
   }
-  const size_t words = H + QKV_ROWS + QS / 2 + H + IM +
-                       static_cast<size_t>(NKV) * MAX_SPLITS * 2 * (HD + 2) + 2 * MAX_CTAS;
-  const size_t ll_bytes = words * sizeof(uint64_t);
-  const size_t total = ll_bytes + 256;
-  void *mem = nullptr;
-  e = cudaMalloc(&mem, total);
-  if (e != cudaSuccess) {
-    fail_msg(5, "cudaMalloc(%zu) for the decode workspace: %s", total, cudaGetErrorString(e));
-    return nullptr;
-  }
-  cudaMemset(mem, 0, total);
+  return sms;
+}
+
+// Lays the Workspace out over `mem` (WS_LL_WORDS + WS_TAIL_WORDS zeroed
+// words) and marks `d` ready.
+void bind_workspace(DevState &d, void *mem, int sms) {
   uint64_t *p = static_cast<uint64_t *>(mem);
   d.ws.hidden = p; p += H;
   d.ws.qkv = p; p += QKV_ROWS;
@@ -1516,7 +1527,7 @@ DevState *get_dev(int *dev_out) {
   d.ws.kv_ready = reinterpret_cast<uint32_t *>(p);
   d.ws.err = reinterpret_cast<unsigned long long *>(p) + 4;
   d.mem = mem;
-  d.ll_bytes = ll_bytes;
+  d.ll_bytes = WS_LL_WORDS * sizeof(uint64_t);
   d.num_sms = sms;
   if (const char *env = getenv("QB200_CTAS")) {
     const int want = atoi(env);
@@ -1524,12 +1535,63 @@ DevState *get_dev(int *dev_out) {
   }
   d.epoch = 1;
   d.ready = true;
+}
+
+// Workspace of the two upstream launchers: allocated on the first call on
+// each device.
+DevState *get_dev(int *dev_out) {
+  if (!current_device(dev_out)) return nullptr;
+  DevState &d = g_dev[*dev_out];
+  if (d.ready) return &d;
+  const int sms = probe_device(*dev_out);
+  if (!sms) return nullptr;
+  const size_t total = (WS_LL_WORDS + WS_TAIL_WORDS) * sizeof(uint64_t);
+  void *mem = nullptr;
+  cudaError_t e = cudaMalloc(&mem, total);
+  if (e != cudaSuccess) {
+    fail_msg(5, "cudaMalloc(%zu) for the decode workspace: %s", total, cudaGetErrorString(e));
+    return nullptr;
+  }
+  cudaMemset(mem, 0, total);
+  bind_workspace(d, mem, sms);
+  return &d;
+}
+
+// Workspace of launch_ldg_generate_nosync_static_ws: the module's static
+// array, looked up once per device (with that device current).  The lookup
+// may load the module on that device and the clearing is a synchronous
+// memset, which is why this set-up belongs before any stream capture.
+// Cleared here because every handoff word must start with an epoch no launch
+// uses (0), and the status word and KV-ready counter at 0.
+DevState g_dev_static[64];
+
+DevState *get_dev_static(int *dev_out) {
+  if (!current_device(dev_out)) return nullptr;
+  DevState &d = g_dev_static[*dev_out];
+  if (d.ready) return &d;
+  const int sms = probe_device(*dev_out);
+  if (!sms) return nullptr;
+  void *mem = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&mem, g_static_ws);
+  if (e != cudaSuccess || mem == nullptr) {
+    fail_msg(6, "cudaGetSymbolAddress(static decode workspace) on device %d: %s", *dev_out,
+             cudaGetErrorString(e));
+    return nullptr;
+  }
+  e = cudaMemset(mem, 0, (WS_LL_WORDS + WS_TAIL_WORDS) * sizeof(uint64_t));
+  if (e != cudaSuccess) {
+    fail_msg(6, "clearing the static decode workspace on device %d: %s", *dev_out,
+             cudaGetErrorString(e));
+    return nullptr;
+  }
+  bind_workspace(d, mem, sms);
   return &d;
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int launch_decode(DecodeArgs &a, cudaStream_t st) {
+// Host-side argument checks shared by every launcher; 0 when accepted.
+int check_args(const DecodeArgs &a) {
   t_err = 0;
   t_msg[0] = 0;
   if (a.num_layers < 1 || a.num_layers > 4096)
@@ -1554,37 +1616,97 @@ int launch_decode(DecodeArgs &a, cudaStream_t st) {
     if (!aligned16(q))
       return fail_msg(14, "layer_weights_packed / weights / KV cache must be 16-byte aligned");
   }
-  std::lock_guard<std::mutex> lk(g_mu);
-  int dev = 0;
-  DevState *d = get_dev(&dev);
-  if (!d) return t_err;
-  if (d->num_sms > MAX_CTAS) return fail_msg(3, "too many SMs");
+  return 0;
+}
+
+// Takes this launch's epochs from `d` and launches on `d`'s workspace.
+int launch_on(DevState &d, DecodeArgs &a, cudaStream_t st) {
+  if (d.num_sms > MAX_CTAS)
+    return fail_msg(3, "%d CTAs requested; the decode workspace holds per-CTA results for at most %d",
+                    d.num_sms, MAX_CTAS);
   const uint64_t need = static_cast<uint64_t>(a.num_steps) * (a.num_layers + 1) + 2;
-  if (static_cast<uint64_t>(d->epoch) + need >= 0xfffffff0ull) {
-    cudaMemsetAsync(d->mem, 0, d->ll_bytes, st);
-    d->epoch = 1;
+  if (static_cast<uint64_t>(d.epoch) + need >= 0xfffffff0ull) {
+    cudaMemsetAsync(d.mem, 0, d.ll_bytes, st);
+    d.epoch = 1;
   }
-  a.epoch_base = d->epoch;
-  d->epoch += static_cast<uint32_t>(need);
-  d->last_tag = a.epoch_base;
+  a.epoch_base = d.epoch;
+  d.epoch += static_cast<uint32_t>(need);
+  d.last_tag = a.epoch_base;
   a.timeout_ns = g_timeout_ns;
-  a.ws = d->ws;
+  a.ws = d.ws;
   a.trace = nullptr;
   a.trace_steps = 0;
   if (g_trace != nullptr) {
-    const long long per_step = static_cast<long long>(d->num_sms) * (a.num_layers + 1) * TR_N * 8;
+    const long long per_step = static_cast<long long>(d.num_sms) * (a.num_layers + 1) * TR_N * 8;
     const long long steps = per_step > 0 ? g_trace_bytes / per_step : 0;
     if (steps > 0) {
       a.trace = g_trace;
       a.trace_steps = static_cast<int>(steps < a.num_steps ? steps : a.num_steps);
     }
   }
-  if (a.num_steps > 1) cudaMemsetAsync(d->ws.kv_ready, 0, sizeof(uint32_t), st);
+  if (a.num_steps > 1) cudaMemsetAsync(d.ws.kv_ready, 0, sizeof(uint32_t), st);
   void *args[] = {&a};
   cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<void *>(decode_kernel),
-                                              dim3(d->num_sms), dim3(NTHREADS), args, smem_bytes(), st);
+                                              dim3(d.num_sms), dim3(NTHREADS), args, smem_bytes(), st);
   if (e != cudaSuccess) return fail_msg(20, "decode kernel launch: %s", cudaGetErrorString(e));
   return 0;
+}
+
+int launch_decode(DecodeArgs &a, cudaStream_t st) {
+  if (check_args(a)) return t_err;
+  std::lock_guard<std::mutex> lk(g_mu);
+  int dev = 0;
+  DevState *d = get_dev(&dev);
+  if (!d) return t_err;
+  return launch_on(*d, a, st);
+}
+
+int launch_decode_static_ws(DecodeArgs &a, cudaStream_t st) {
+  if (check_args(a)) return t_err;
+  std::lock_guard<std::mutex> lk(g_mu);
+  int dev = 0;
+  DevState *d = get_dev_static(&dev);
+  if (!d) return t_err;
+  return launch_on(*d, a, st);
+}
+
+// Kernel arguments of a generate call (parameters as launch_ldg_generate_nosync).
+DecodeArgs generate_args(int first_token_id, int num_steps, const void *embed_weight,
+                         const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+                         const void *lm_head_weight, const void *cos_table, const void *sin_table,
+                         void *k_cache, void *v_cache, void *hidden_buffer, void *g_activations,
+                         void *g_residual, void *g_q, void *g_k, void *g_v, void *g_attn_out,
+                         void *g_mlp_intermediate, void *g_normalized, void *block_max_vals,
+                         void *block_max_idxs, int *output_log, int num_layers, int start_position,
+                         int max_seq_len, float attn_scale) {
+  DecodeArgs a{};
+  a.embed = static_cast<const __half *>(embed_weight);
+  a.layers = layer_weights;
+  a.final_norm = static_cast<const __half *>(final_norm_weight);
+  a.lm_head = static_cast<const __half *>(lm_head_weight);
+  a.cos_t = static_cast<const __half *>(cos_table);
+  a.sin_t = static_cast<const __half *>(sin_table);
+  a.k_cache = static_cast<__half *>(k_cache);
+  a.v_cache = static_cast<__half *>(v_cache);
+  a.hidden = static_cast<__half *>(hidden_buffer);
+  a.act = static_cast<float *>(g_activations);
+  a.res = static_cast<float *>(g_residual);
+  a.q = static_cast<__half *>(g_q);
+  a.k = static_cast<__half *>(g_k);
+  a.v = static_cast<__half *>(g_v);
+  a.attn_out = static_cast<__half *>(g_attn_out);
+  a.inter = static_cast<float *>(g_mlp_intermediate);
+  a.norm_out = static_cast<float *>(g_normalized);
+  a.bmax_vals = static_cast<float *>(block_max_vals);
+  a.bmax_idxs = static_cast<int *>(block_max_idxs);
+  a.out_tokens = output_log;
+  a.num_layers = num_layers;
+  a.start_pos = start_position;
+  a.max_seq = max_seq_len;
+  a.num_steps = num_steps;
+  a.first_token = first_token_id;
+  a.attn_scale = attn_scale;
+  return a;
 }
 
 }  // namespace
@@ -1679,34 +1801,30 @@ void launch_ldg_generate_nosync(int first_token_id, int num_steps, const void *e
                                 void *block_max_idxs, int *output_log, int num_layers,
                                 int start_position, int max_seq_len, float attn_scale,
                                 void *stream) {
-  DecodeArgs a{};
-  a.embed = static_cast<const __half *>(embed_weight);
-  a.layers = layer_weights;
-  a.final_norm = static_cast<const __half *>(final_norm_weight);
-  a.lm_head = static_cast<const __half *>(lm_head_weight);
-  a.cos_t = static_cast<const __half *>(cos_table);
-  a.sin_t = static_cast<const __half *>(sin_table);
-  a.k_cache = static_cast<__half *>(k_cache);
-  a.v_cache = static_cast<__half *>(v_cache);
-  a.hidden = static_cast<__half *>(hidden_buffer);
-  a.act = static_cast<float *>(g_activations);
-  a.res = static_cast<float *>(g_residual);
-  a.q = static_cast<__half *>(g_q);
-  a.k = static_cast<__half *>(g_k);
-  a.v = static_cast<__half *>(g_v);
-  a.attn_out = static_cast<__half *>(g_attn_out);
-  a.inter = static_cast<float *>(g_mlp_intermediate);
-  a.norm_out = static_cast<float *>(g_normalized);
-  a.bmax_vals = static_cast<float *>(block_max_vals);
-  a.bmax_idxs = static_cast<int *>(block_max_idxs);
-  a.out_tokens = output_log;
-  a.num_layers = num_layers;
-  a.start_pos = start_position;
-  a.max_seq = max_seq_len;
-  a.num_steps = num_steps;
-  a.first_token = first_token_id;
-  a.attn_scale = attn_scale;
+  DecodeArgs a = generate_args(first_token_id, num_steps, embed_weight, layer_weights,
+                               final_norm_weight, lm_head_weight, cos_table, sin_table, k_cache,
+                               v_cache, hidden_buffer, g_activations, g_residual, g_q, g_k, g_v,
+                               g_attn_out, g_mlp_intermediate, g_normalized, block_max_vals,
+                               block_max_idxs, output_log, num_layers, start_position,
+                               max_seq_len, attn_scale);
   launch_decode(a, static_cast<cudaStream_t>(stream));
+}
+
+int launch_ldg_generate_nosync_static_ws(
+    int first_token_id, int num_steps, const void *embed_weight,
+    const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table, void *k_cache,
+    void *v_cache, void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+    void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate, void *g_normalized,
+    void *block_max_vals, void *block_max_idxs, int *output_log, int num_layers,
+    int start_position, int max_seq_len, float attn_scale, void *stream) {
+  DecodeArgs a = generate_args(first_token_id, num_steps, embed_weight, layer_weights,
+                               final_norm_weight, lm_head_weight, cos_table, sin_table, k_cache,
+                               v_cache, hidden_buffer, g_activations, g_residual, g_q, g_k, g_v,
+                               g_attn_out, g_mlp_intermediate, g_normalized, block_max_vals,
+                               block_max_idxs, output_log, num_layers, start_position,
+                               max_seq_len, attn_scale);
+  return launch_decode_static_ws(a, static_cast<cudaStream_t>(stream));
 }
 
 int qwen_b200_selftest_wait_timeout(long long timeout_ns, void *stream) {
