@@ -145,11 +145,12 @@ def test_oracle_matches_upstream_ops():
         reff = torch.from_numpy(g[f"rmsf_out_{b}"].view(np.float16))
         assert (outf == reff).float().mean() > 0.999
         if b in OPS_CASE["swiglu_batches"]:
-            xs = out.view(b, 1, 1024)
+            # Same input as upstream's run: its own RMSNorm output.  The
+            # sequential fp16 accumulation is restated exactly: bit-equal.
+            xs = ref.view(b, 1, 1024)
             y = O.swiglu_forward_down(xs, wg, wu, wd)
             refy = torch.from_numpy(g[f"swd_out_{b}"].view(np.float16)).view_as(y)
-            assert (y == refy).float().mean() > 0.99, "fp16-accumulation restatement drifted"
-            assert float((y.float() - refy.float()).abs().max()) < 1e-2
+            assert torch.equal(y, refy), "fp16-accumulation restatement drifted"
             f, _, _ = O.swiglu_forward(xs, wg, wu)
             reff = torch.from_numpy(g[f"swf_out_{b}"].view(np.float16)).view_as(f)
-            assert (f == reff).float().mean() > 0.99
+            assert torch.equal(f, reff)
