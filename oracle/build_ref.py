@@ -58,6 +58,12 @@ def build(ref: str) -> bool:
         print(f"[build_ref] reference checkout not found at {ref}; skipping")
         return False
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
+    # The image's CXX / CC wrapper links a static C++ runtime that crashes
+    # on stream formatting next to torch's shared libstdc++; use the system
+    # compilers, as the package build does.
+    for var, path in (("CXX", "/usr/bin/g++"), ("CC", "/usr/bin/gcc")):
+        if os.path.exists(path):
+            os.environ[var] = path
     os.makedirs(OUT, exist_ok=True)
     t = os.path.join(ref, "Tools")
     mk, rn, sw = (os.path.join(t, d) for d in ("megakernel", "rmsnorm", "swiglu"))

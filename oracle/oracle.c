@@ -316,15 +316,22 @@ void oracle_rmsnorm(const half_t *input, const half_t *weight, half_t *residual,
     half_t *o = out + (size_t)r * cols;
     float ss = 0.f;
     if (residual) {
+      /* Elements below (cols/4)*4 take the vector path (rmsnorm.cuh:47-62,
+       * :82-93), the rest the scalar remainder path (:64-69, :95-99), which
+       * squares the unrounded sum and normalises as (res*inv)*w. */
+      const int vec_end = (cols / 4) * 4;
       half_t *res = residual + (size_t)r * cols;
       for (int i = 0; i < cols; i++) {
-        res[i] = f2h(h2f(x[i]) + h2f(res[i]));           /* __hadd2 */
-        float f = h2f(res[i]);
+        const float sum = h2f(x[i]) + h2f(res[i]);
+        res[i] = f2h(sum);                                  /* __hadd2 / static_cast<T> */
+        const float f = i < vec_end ? h2f(res[i]) : sum;
         ss = fmaf(f, f, ss);
       }
       float inv = rsqrt_ref(ss / (float)cols + eps);
       rms_out[r] = 1.0f / inv;
-      for (int i = 0; i < cols; i++) o[i] = f2h(h2f(res[i]) * (inv * h2f(weight[i])));
+      for (int i = 0; i < cols; i++)
+        o[i] = i < vec_end ? f2h(h2f(res[i]) * (inv * h2f(weight[i])))
+                           : f2h(h2f(res[i]) * inv * h2f(weight[i]));
     } else {
       for (int i = 0; i < cols; i++) {
         float f = h2f(x[i]);
@@ -346,17 +353,18 @@ static inline float silu_c10(float x) { return rh(x / (1.0f + expf(-x))); }
 
 /*
  * SwiGLU forward, Tools/swiglu/swiglu.cu:89-130 with T = c10::Half:
- * out[row, i] = silu(x.Wg[:,i]) * (x.Wu[:,i]), fp16 accumulation in h order.
+ * out[row, i] = silu(x.Wg[:,i]) * (x.Wu[:,i]), fp16 accumulation in h order
+ * starting from the bias (swiglu.cu:111-112; 0 when bg / bu are NULL).
  * Weights use the upstream [H, I] layout.  gate_cache / up_cache may be NULL.
  */
-void oracle_swiglu_forward(const half_t *x, const half_t *wg, const half_t *wu, int rows,
-                           int hidden, int inter, half_t *out, half_t *gate_cache,
-                           half_t *up_cache, int nthreads) {
+void oracle_swiglu_forward(const half_t *x, const half_t *wg, const half_t *wu, const half_t *bg,
+                           const half_t *bu, int rows, int hidden, int inter, half_t *out,
+                           half_t *gate_cache, half_t *up_cache, int nthreads) {
   set_threads(nthreads);
 #pragma omp parallel for schedule(static) collapse(2)
   for (int r = 0; r < rows; r++) {
     for (int i = 0; i < inter; i++) {
-      float g = 0.f, u = 0.f;
+      float g = bg ? h2f(bg[i]) : 0.f, u = bu ? h2f(bu[i]) : 0.f;
       for (int h = 0; h < hidden; h++) {
         float xv = h2f(x[(size_t)r * hidden + h]);
         g = hadd_c10(g, hmul_c10(xv, h2f(wg[(size_t)h * inter + i])));
@@ -378,14 +386,15 @@ void oracle_swiglu_forward(const half_t *x, const half_t *wg, const half_t *wu, 
  * operations the upstream kernel repeats per column.
  */
 void oracle_swiglu_forward_down(const half_t *x, const half_t *wg, const half_t *wu,
-                                const half_t *wd, int rows, int hidden, int inter, half_t *out,
+                                const half_t *wd, const half_t *bg, const half_t *bu,
+                                const half_t *bd, int rows, int hidden, int inter, half_t *out,
                                 int nthreads) {
   set_threads(nthreads);
   float *so = (float *)malloc(sizeof(float) * (size_t)rows * inter);
 #pragma omp parallel for schedule(static) collapse(2)
   for (int r = 0; r < rows; r++) {
     for (int i = 0; i < inter; i++) {
-      float g = 0.f, u = 0.f;
+      float g = bg ? h2f(bg[i]) : 0.f, u = bu ? h2f(bu[i]) : 0.f;
       for (int h = 0; h < hidden; h++) {
         float xv = h2f(x[(size_t)r * hidden + h]);
         g = hadd_c10(g, hmul_c10(xv, h2f(wg[(size_t)h * inter + i])));
@@ -397,7 +406,7 @@ void oracle_swiglu_forward_down(const half_t *x, const half_t *wg, const half_t 
 #pragma omp parallel for schedule(static) collapse(2)
   for (int r = 0; r < rows; r++) {
     for (int h = 0; h < hidden; h++) {
-      float acc = 0.f;
+      float acc = bd ? h2f(bd[h]) : 0.f;
       for (int i = 0; i < inter; i++)
         acc = hadd_c10(acc, hmul_c10(so[(size_t)r * inter + i], h2f(wd[(size_t)i * hidden + h])));
       out[(size_t)r * hidden + h] = f2h(acc);

@@ -52,9 +52,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_rmsnorm.restype = None
         L.oracle_rmsnorm.argtypes = [vp, vp, vp, vp, vp, i, i, f]
         L.oracle_swiglu_forward.restype = None
-        L.oracle_swiglu_forward.argtypes = [vp, vp, vp, i, i, i, vp, vp, vp, i]
+        L.oracle_swiglu_forward.argtypes = [vp, vp, vp, vp, vp, i, i, i, vp, vp, vp, i]
         L.oracle_swiglu_forward_down.restype = None
-        L.oracle_swiglu_forward_down.argtypes = [vp, vp, vp, vp, i, i, i, vp, i]
+        L.oracle_swiglu_forward_down.argtypes = [vp, vp, vp, vp, vp, vp, vp, i, i, i, vp, i]
         L.oracle_silu_half.restype = f
         L.oracle_silu_half.argtypes = [f]
         _lib = L
@@ -151,24 +151,34 @@ def rmsnorm_forward(x: torch.Tensor, w: torch.Tensor, eps: float,
     return out, rms
 
 
-def swiglu_forward(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, nthreads: int = 0):
-    """``swiglu_fused.forward`` (swiglu.cu:316-361): x [B,S,H], W [H,I]."""
+def _opt(t: torch.Tensor | None) -> torch.Tensor | None:
+    return None if t is None else t.cpu().contiguous()
+
+
+def swiglu_forward(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
+                   b_gate: torch.Tensor | None = None, b_up: torch.Tensor | None = None,
+                   nthreads: int = 0):
+    """``swiglu_fused.forward`` (swiglu.cu:316-361): x [B,S,H], W [H,I], biases [I] or None."""
     b, s, h = x.shape
     inter = wg.shape[1]
     out = torch.empty(b, s, inter, dtype=torch.float16)
     gc, uc = torch.empty_like(out), torch.empty_like(out)
+    bg, bu = _opt(b_gate), _opt(b_up)
     lib().oracle_swiglu_forward(_ptr(x.contiguous()), _ptr(wg.contiguous()), _ptr(wu.contiguous()),
-                                b * s, h, inter, _ptr(out), _ptr(gc), _ptr(uc), nthreads)
+                                _ptr(bg), _ptr(bu), b * s, h, inter, _ptr(out), _ptr(gc), _ptr(uc),
+                                nthreads)
     return out, gc, uc
 
 
 def swiglu_forward_down(x: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor,
-                        nthreads: int = 0) -> torch.Tensor:
-    """``swiglu_fused.forward_down`` (swiglu.cu:413-464): Wg, Wu [H,I], Wd [I,H]."""
+                        b_gate: torch.Tensor | None = None, b_up: torch.Tensor | None = None,
+                        b_down: torch.Tensor | None = None, nthreads: int = 0) -> torch.Tensor:
+    """``swiglu_fused.forward_down`` (swiglu.cu:413-464): Wg, Wu [H,I], Wd [I,H], biases or None."""
     b, s, h = x.shape
     inter = wg.shape[1]
     out = torch.empty(b, s, h, dtype=torch.float16)
+    bg, bu, bd = _opt(b_gate), _opt(b_up), _opt(b_down)
     lib().oracle_swiglu_forward_down(_ptr(x.contiguous()), _ptr(wg.contiguous()),
-                                     _ptr(wu.contiguous()), _ptr(wd.contiguous()), b * s, h,
-                                     inter, _ptr(out), nthreads)
+                                     _ptr(wu.contiguous()), _ptr(wd.contiguous()), _ptr(bg),
+                                     _ptr(bu), _ptr(bd), b * s, h, inter, _ptr(out), nthreads)
     return out

@@ -29,6 +29,8 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", GENCODE, "-Xcompiler", "-fPIC", 
 # Python extension modules: name -> C++ sources (in csrc/).
 EXTENSIONS = {
     "qwen_megakernel_C": ["qwen_ops.cpp"],
+    "rmsnorm": ["rmsnorm_ops.cpp"],
+    "swiglu_fused": ["swiglu_ops.cpp"],
 }
 
 
@@ -44,7 +46,8 @@ def _newest(paths) -> float:
 
 def build_native(force: bool = False, verbose: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    deps = srcs + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
+    deps = (srcs + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
+            + glob.glob(os.path.join(INCLUDE, "*.h")))
     if not force and os.path.exists(LIB) and os.path.getmtime(LIB) >= _newest(deps):
         return LIB
     tmp = LIB + ".tmp"
@@ -57,6 +60,17 @@ def build_native(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+def use_system_host_compiler() -> None:
+    """Build torch extensions with the system g++/gcc.  The image's CXX / CC
+    point at a GCC wrapper that links its own static C++ runtime; an extension
+    built that way crashes as soon as it formats a number into a C++ stream
+    (every TORCH_CHECK message with a size in it), because the stream code
+    meets the shared libstdc++ that torch has loaded."""
+    for var, path in (("CXX", "/usr/bin/g++"), ("CC", "/usr/bin/gcc")):
+        if os.path.exists(path):
+            os.environ[var] = path
+
+
 def build_extension(name: str, force: bool = False, verbose: bool = False) -> str:
     srcs = [os.path.join(CSRC, s) for s in EXTENSIONS[name]]
     dst = os.path.join(PKG, f"{name}.so")
@@ -65,6 +79,7 @@ def build_extension(name: str, force: bool = False, verbose: bool = False) -> st
         return dst
     from torch.utils.cpp_extension import load
 
+    use_system_host_compiler()
     workdir = os.path.join(PKG, "_build", name)
     os.makedirs(workdir, exist_ok=True)
     load(

@@ -1390,7 +1390,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte aligned base: the padded row layout relies on slot bases that
   // are multiples of 128 bytes.
-  Smem &sm = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  // Offset the shared array itself rather than an integer copy of its
+  // address: the compiler then keeps every Smem access in the shared address
+  // space (LDS/STS instead of generic loads and stores).
+  Smem &sm = *reinterpret_cast<Smem *>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
   const int tid = threadIdx.x;
   if (tid == 0) {
     for (int i = 0; i < NSLOTS; ++i) {
@@ -1714,6 +1717,15 @@ DecodeArgs generate_args(int first_token_id, int num_steps, const void *embed_we
 extern "C" {
 
 int qwen_b200_abi_version(void) { return QWEN_B200_ABI_VERSION; }
+
+// Shared with the operator library (ops.cu): one thread-local error slot for
+// every entry point of this library.
+void qb200_clear_error(void) {
+  t_err = 0;
+  t_msg[0] = 0;
+}
+
+int qb200_set_error(int code, const char *msg) { return fail_msg(code, "%s", msg); }
 
 int qwen_b200_last_error(char *msg, int msg_len) {
   if (msg && msg_len > 0) {

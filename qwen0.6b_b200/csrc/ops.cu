@@ -1,0 +1,572 @@
+// ops.cu - standalone RMSNorm and SwiGLU operators for B200 (sm_100a): the
+// replacements of the upstream Tools/rmsnorm and Tools/swiglu extensions, with
+// the C ABI of include/qwen_b200_ops.h.
+//
+// RMSNorm (rmsnorm.cuh:17-176): one warp per row, 16-byte loads, fp32 sum of
+// squares, the upstream rounding points.  Memory-bound and tiny.
+//
+// SwiGLU (swiglu.cu:89-130, :267-310): upstream accumulates in c10::Half, so
+// every product and every partial sum is rounded to fp16 in ascending index
+// order.  That makes each output a serial chain over the reduction index that
+// cannot be reassociated, split or put on tensor cores without changing the
+// result.  The B200 design keeps the chain exact and restructures everything
+// around it:
+//  * one "chain GEMM" kernel, C[r, n] = init[n] (+)= A[r, k] (*) B[k, n] with
+//    fp16-rounded (*) and (+), k ascending; used for gate/up (two B matrices
+//    sharing the A loads, SiLU epilogue) and for down;
+//  * the SwiGLU activations are computed once per row and reused by every
+//    down-projection output (upstream recomputes them per output element,
+//    O(rows * hidden^2 * inter));
+//  * A and B tiles are streamed through a 4-stage shared-memory ring by TMA
+//    tensor copies (one producer lane, mbarrier completion, no multicast), so
+//    weight bytes stay in flight while the chains run;
+//  * each thread carries two adjacent output columns as one half2 chain
+//    (gate and up: two half2 chains), using the non-contracting
+//    __hmul2_rn / __hadd2_rn so products are never fused into an FMA.
+// The chain latency (reduction length x dependent fp16 add latency) bounds a
+// small-batch call; the fp16 ALU issue rate bounds a large-batch one.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "host_err.h"
+#include "ptx.cuh"
+#include "qwen_b200_ops.h"
+
+namespace qb200ops {
+
+using qb200::fence_mbar_init;
+using qb200::globaltimer_ns;
+using qb200::mbar_arrive;
+using qb200::mbar_arrive_expect_tx;
+using qb200::mbar_init;
+using qb200::mbar_try_wait;
+using qb200::smem_u32;
+
+constexpr int RB = 16;                  // rows per tile
+constexpr int CB = 16;                  // output columns per tile
+constexpr int KC = 128;                 // reduction chunk per ring stage
+constexpr int NST = 4;                  // ring stages
+constexpr int CONS_WARPS = 4;           // RB rows x CB/2 column pairs = 128 threads
+constexpr int CONS_THREADS = CONS_WARPS * 32;
+constexpr int THREADS = CONS_THREADS + 32;  // + producer warp
+constexpr int A_BYTES = RB * KC * 2;    // TMA box {KC, RB} of A [rows, K]
+constexpr int B_BYTES = KC * CB * 2;    // TMA box {CB, KC} of B [K, N]
+constexpr int MAX_ROW_TILES = 65535;
+constexpr long long WAIT_NS = 2000000000LL;
+
+constexpr uint32_t ERR_FULL_WAIT = 1, ERR_EMPTY_WAIT = 2, ERR_DRAIN_WAIT = 3;
+
+// Status word of the operator kernels: (code << 32) | (blockIdx.y << 16) | blockIdx.x
+// of the first bounded wait that gave up.
+__device__ unsigned long long g_ops_err = 0;
+
+struct ChainArgs {
+  const __half *init0;  // [N] start values of chain 0 (bias) or nullptr (+0)
+  const __half *init1;  // [N] start values of chain 1 (DUAL) or nullptr
+  __half *out;          // [rows, N]
+  __half *cache0;       // DUAL: [rows, N] final chain-0 values (gate) or nullptr
+  __half *cache1;       // DUAL: [rows, N] final chain-1 values (up) or nullptr
+  int rows, K, N;
+};
+
+template <bool DUAL>
+constexpr int stage_bytes() {
+  return A_BYTES + B_BYTES * (DUAL ? 2 : 1);
+}
+
+template <bool DUAL>
+constexpr size_t chain_smem_bytes() {
+  return static_cast<size_t>(NST) * stage_bytes<DUAL>() + 2 * NST * sizeof(uint64_t) + 16 + 1024;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __noinline__ void record_error(uint32_t code) {
+  const unsigned long long v = (static_cast<unsigned long long>(code) << 32) |
+                               (static_cast<unsigned long long>(blockIdx.y & 0xffffu) << 16) |
+                               (blockIdx.x & 0xffffu);
+  atomicCAS(&g_ops_err, 0ull, v);
+}
+
+// Bounded mbarrier wait: gives up after WAIT_NS or when the CTA's abort flag
+// is set; the first thread to give up records the error and sets the flag.
+__device__ __noinline__ bool wait_bar_slow(uint64_t *bar, uint32_t parity,
+                                           volatile uint32_t *abort, uint32_t code) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
+      *abort = 1;
+      record_error(code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
+                                         uint32_t code) {
+  return mbar_try_wait(bar, parity) || wait_bar_slow(bar, parity, abort, code);
+}
+
+// c10::Half SiLU as upstream instantiates it (swiglu.cu:60-63): the Half
+// operand is widened, x / (1 + expf(-x)) evaluated in fp32, rounded on return.
+__device__ __forceinline__ __half silu_c10(__half x) {
+  const float xf = __half2float(x);
+  return __float2half_rn(xf / (1.0f + expf(-xf)));
+}
+
+// grid (ceil(N / CB), ceil(rows / RB)), THREADS threads, chain_smem_bytes<DUAL>().
+template <bool DUAL>
+__global__ void __launch_bounds__(THREADS)
+    chain_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_b0,
+                      const __grid_constant__ CUtensorMap tm_b1, const ChainArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Offset the array itself (not an integer copy of its address), so that
+  // the compiler keeps every access in the shared address space (LDS/STS,
+  // not generic loads).
+  uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr int SB = stage_bytes<DUAL>();
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + NST * SB);
+  uint64_t *empty = full + NST;
+  volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(empty + NST);
+
+  const int tid = threadIdx.x;
+  const int nchunks = (p.K + KC - 1) / KC;
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CONS_WARPS);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (tid >= CONS_THREADS) {
+    // Producer: one lane streams A and B chunks into the ring.
+    if (tid != CONS_THREADS) return;
+    int issued = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c % NST;
+      if (c >= NST && !wait_bar(&empty[s], ((c / NST) - 1) & 1, abort, ERR_EMPTY_WAIT)) break;
+      uint8_t *st = base + s * SB;
+      mbar_arrive_expect_tx(&full[s], SB);
+      tma_load_2d(st, &tm_a, c * KC, blockIdx.y * RB, &full[s]);
+      tma_load_2d(st + A_BYTES, &tm_b0, blockIdx.x * CB, c * KC, &full[s]);
+      if constexpr (DUAL) tma_load_2d(st + A_BYTES + B_BYTES, &tm_b1, blockIdx.x * CB, c * KC, &full[s]);
+      issued = c + 1;
+    }
+    // Let every issued copy land before the CTA can exit.
+    for (int c = (issued > NST ? issued - NST : 0); c < issued; ++c) {
+      const int s = c % NST;
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[s], (c / NST) & 1)) {
+        if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
+          record_error(ERR_DRAIN_WAIT);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // Consumers: thread = (row in tile, column pair).
+  const int lane = tid & 31;
+  const int cp = tid & 7, rl = tid >> 3;
+  const int r = blockIdx.y * RB + rl;
+  const int n = blockIdx.x * CB + 2 * cp;
+  const bool active = r < p.rows && n < p.N;  // N is even, so n + 1 < N too
+  const __half2 zero = __float2half2_rn(0.0f);
+  __half2 acc0 = (p.init0 != nullptr && n < p.N) ? *reinterpret_cast<const __half2 *>(p.init0 + n) : zero;
+  __half2 acc1 = zero;
+  if constexpr (DUAL) {
+    if (p.init1 != nullptr && n < p.N) acc1 = *reinterpret_cast<const __half2 *>(p.init1 + n);
+  }
+  for (int c = 0; c < nchunks; ++c) {
+    const int s = c % NST;
+    if (!wait_bar(&full[s], (c / NST) & 1, abort, ERR_FULL_WAIT)) return;
+    const int kn = min(KC, p.K - c * KC);  // a multiple of 8
+    if (active) {
+      const uint8_t *st = base + s * SB;
+      const __half *arow = reinterpret_cast<const __half *>(st) + rl * KC;
+      const __half2 *b0 = reinterpret_cast<const __half2 *>(st + A_BYTES) + cp;
+      const __half2 *b1 = reinterpret_cast<const __half2 *>(st + A_BYTES + B_BYTES) + cp;
+#pragma unroll 2
+      for (int k = 0; k < kn; k += 8) {
+        const uint4 av = *reinterpret_cast<const uint4 *>(arow + k);
+        const __half *ah = reinterpret_cast<const __half *>(&av);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const __half2 x2 = __half2half2(ah[j]);
+          acc0 = __hadd2_rn(acc0, __hmul2_rn(x2, b0[(k + j) * (CB / 2)]));
+          if constexpr (DUAL) acc1 = __hadd2_rn(acc1, __hmul2_rn(x2, b1[(k + j) * (CB / 2)]));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (!active) return;
+  const size_t o = static_cast<size_t>(r) * p.N + n;
+  if constexpr (DUAL) {
+    const __half g0 = __low2half(acc0), g1 = __high2half(acc0);
+    const __half u0 = __low2half(acc1), u1 = __high2half(acc1);
+    *reinterpret_cast<__half2 *>(p.out + o) =
+        __halves2half2(__hmul_rn(silu_c10(g0), u0), __hmul_rn(silu_c10(g1), u1));
+    if (p.cache0 != nullptr) *reinterpret_cast<__half2 *>(p.cache0 + o) = acc0;
+    if (p.cache1 != nullptr) *reinterpret_cast<__half2 *>(p.cache1 + o) = acc1;
+  } else {
+    *reinterpret_cast<__half2 *>(p.out + o) = acc0;
+  }
+}
+
+// RMSNorm, one warp per row (8 rows per 256-thread CTA).  With `res`, the
+// fused form: res = half(x + res) written back, then normalise res.
+// Elements below (cols / 4) * 4 follow upstream's vector path, the rest its
+// scalar remainder path (rmsnorm.cuh:47-76, :95-108), whose rounding differs.
+__global__ void __launch_bounds__(256)
+    rmsnorm_kernel(__half *__restrict__ out, float *__restrict__ rms,
+                   const __half *__restrict__ x, const __half *__restrict__ w,
+                   __half *__restrict__ res, long long rows, int cols, float eps) {
+  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __half *xr = x + row * cols;
+  __half *rr = res != nullptr ? res + row * cols : nullptr;
+  __half *orow = out + row * cols;
+  float ss = 0.0f;
+  if ((cols & 7) == 0) {
+    const int nv = cols >> 3;
+    for (int i = lane; i < nv; i += 32) {
+      uint4 v = reinterpret_cast<const uint4 *>(xr)[i];
+      __half2 *h = reinterpret_cast<__half2 *>(&v);
+      if (rr != nullptr) {
+        uint4 rv = reinterpret_cast<const uint4 *>(rr)[i];
+        const __half2 *hr = reinterpret_cast<const __half2 *>(&rv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __hadd2_rn(h[j], hr[j]);
+        reinterpret_cast<uint4 *>(rr)[i] = v;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+  } else {
+    const int vec_end = (cols >> 2) << 2;
+    for (int i = lane; i < cols; i += 32) {
+      float v;
+      if (rr != nullptr) {
+        const float sum = __half2float(xr[i]) + __half2float(rr[i]);
+        rr[i] = __float2half_rn(sum);
+        v = i < vec_end ? __half2float(rr[i]) : sum;
+      } else {
+        v = __half2float(xr[i]);
+      }
+      ss = fmaf(v, v, ss);
+    }
+  }
+  ss = qb200::warp_sum(ss);
+  const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+  if (lane == 0) rms[row] = 1.0f / inv;
+  const __half *src = rr != nullptr ? rr : xr;
+  if ((cols & 7) == 0) {
+    const int nv = cols >> 3;
+    for (int i = lane; i < nv; i += 32) {
+      uint4 v = reinterpret_cast<const uint4 *>(src)[i];
+      const uint4 wv = reinterpret_cast<const uint4 *>(w)[i];
+      __half2 *h = reinterpret_cast<__half2 *>(&v);
+      const __half2 *hw = reinterpret_cast<const __half2 *>(&wv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        const float2 g = __half22float2(hw[j]);
+        if (rr != nullptr)
+          h[j] = __floats2half2_rn(__fmul_rn(f.x, __fmul_rn(inv, g.x)), __fmul_rn(f.y, __fmul_rn(inv, g.y)));
+        else
+          h[j] = __floats2half2_rn(__fmul_rn(__fmul_rn(f.x, inv), g.x), __fmul_rn(__fmul_rn(f.y, inv), g.y));
+      }
+      reinterpret_cast<uint4 *>(orow)[i] = v;
+    }
+  } else {
+    const int vec_end = (cols >> 2) << 2;
+    for (int i = lane; i < cols; i += 32) {
+      const float f = __half2float(src[i]);
+      const float g = __half2float(w[i]);
+      const bool vec_form = rr != nullptr && i < vec_end;
+      orow[i] = __float2half_rn(vec_form ? __fmul_rn(f, __fmul_rn(inv, g)) : __fmul_rn(__fmul_rn(f, inv), g));
+    }
+  }
+}
+
+}  // namespace qb200ops
+
+// ====================================================================== host
+using namespace qb200ops;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_ops_mu;
+EncodeTiledFn g_encode = nullptr;
+bool g_attr_set[64][2] = {};
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return qb200_set_error(code, buf);
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+EncodeTiledFn encoder() {
+  std::lock_guard<std::mutex> lk(g_ops_mu);
+  if (g_encode == nullptr) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  return g_encode;
+}
+
+// 2-D fp16 row-major [outer, inner] tensor, box {box_inner, box_outer}, zero fill.
+int make_map(CUtensorMap *m, const void *ptr, long long inner, long long outer, int box_inner,
+             int box_outer) {
+  EncodeTiledFn enc = encoder();
+  if (enc == nullptr) return fail(30, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(31, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return 0;
+}
+
+template <bool DUAL>
+int ensure_attr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(2, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> lk(g_ops_mu);
+  if (!g_attr_set[dev][DUAL]) {
+    const cudaError_t e = cudaFuncSetAttribute(chain_gemm_kernel<DUAL>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(chain_smem_bytes<DUAL>()));
+    if (e != cudaSuccess) return fail(4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    g_attr_set[dev][DUAL] = true;
+  }
+  return 0;
+}
+
+// C[rows, N] = chain(A[rows, K], B0[K, N] (, B1)).
+template <bool DUAL>
+int launch_chain(const __half *a, const __half *b0, const __half *b1, const ChainArgs &args,
+                 cudaStream_t st) {
+  if (int rc = ensure_attr<DUAL>()) return rc;
+  CUtensorMap ma, mb0, mb1;
+  if (int rc = make_map(&ma, a, args.K, args.rows, KC, RB)) return rc;
+  if (int rc = make_map(&mb0, b0, args.N, args.K, CB, KC)) return rc;
+  if (DUAL) {
+    if (int rc = make_map(&mb1, b1, args.N, args.K, CB, KC)) return rc;
+  } else {
+    mb1 = mb0;
+  }
+  const dim3 grid((args.N + CB - 1) / CB, (args.rows + RB - 1) / RB);
+  chain_gemm_kernel<DUAL><<<grid, THREADS, chain_smem_bytes<DUAL>(), st>>>(ma, mb0, mb1, args);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "SwiGLU kernel launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+int check_swiglu(const void *x, const void *wg, const void *wu, const void *wd, const void *bg,
+                 const void *bu, const void *bd, long long rows, int hidden, int inter) {
+  if (rows < 0 || rows > static_cast<long long>(MAX_ROW_TILES) * RB)
+    return fail(10, "rows=%lld out of range [0, %d]", rows, MAX_ROW_TILES * RB);
+  if (hidden <= 0 || inter <= 0 || (hidden & 7) || (inter & 7))
+    return fail(10, "hidden=%d and inter=%d must be positive multiples of 8", hidden, inter);
+  if (rows == 0) return 0;  // nothing to read or write; empty tensors may have null pointers
+  if (x == nullptr || wg == nullptr || wu == nullptr) return fail(13, "null pointer argument");
+  for (const void *q : {x, wg, wu, wd, bg, bu, bd})
+    if (q != nullptr && !al16(q)) return fail(14, "SwiGLU operands must be 16-byte aligned");
+  return 0;
+}
+
+long long round256(long long b) { return (b + 255) & ~255ll; }
+
+int rmsnorm_launch(void *out, float *rms, const void *input, const void *weight, void *residual,
+                   long long rows, int cols, float eps, cudaStream_t st) {
+  if (rows < 0 || cols <= 0) return fail(10, "rows=%lld cols=%d out of range", rows, cols);
+  if (rows == 0) return 0;
+  if (out == nullptr || rms == nullptr || input == nullptr || weight == nullptr)
+    return fail(13, "null pointer argument");
+  if ((cols & 7) == 0) {
+    for (const void *q : {static_cast<const void *>(out), input, weight,
+                          static_cast<const void *>(residual)})
+      if (q != nullptr && !al16(q)) return fail(14, "RMSNorm operands must be 16-byte aligned");
+  }
+  const long long blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffffll) return fail(10, "rows=%lld too large", rows);
+  rmsnorm_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<__half *>(out), rms, static_cast<const __half *>(input),
+      static_cast<const __half *>(weight), static_cast<__half *>(residual), rows, cols, eps);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "RMSNorm kernel launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+int swiglu_forward_launch(const void *x, const void *wg, const void *wu, const void *bg,
+                          const void *bu, void *out, void *gc, void *uc, long long rows,
+                          int hidden, int inter, cudaStream_t st) {
+  ChainArgs a{};
+  a.init0 = static_cast<const __half *>(bg);
+  a.init1 = static_cast<const __half *>(bu);
+  a.out = static_cast<__half *>(out);
+  a.cache0 = static_cast<__half *>(gc);
+  a.cache1 = static_cast<__half *>(uc);
+  a.rows = static_cast<int>(rows);
+  a.K = hidden;
+  a.N = inter;
+  return launch_chain<true>(static_cast<const __half *>(x), static_cast<const __half *>(wg),
+                            static_cast<const __half *>(wu), a, st);
+}
+
+int down_launch(const void *s, const void *wd, const void *bd, void *out, long long rows,
+                int hidden, int inter, cudaStream_t st) {
+  ChainArgs a{};
+  a.init0 = static_cast<const __half *>(bd);
+  a.out = static_cast<__half *>(out);
+  a.rows = static_cast<int>(rows);
+  a.K = inter;
+  a.N = hidden;
+  const __half *wdh = static_cast<const __half *>(wd);
+  return launch_chain<false>(static_cast<const __half *>(s), wdh, wdh, a, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_b200_rmsnorm_forward(void *out, float *rms, const void *input, const void *weight,
+                              void *residual, long long rows, int cols, float eps, void *stream) {
+  qb200_clear_error();
+  return rmsnorm_launch(out, rms, input, weight, residual, rows, cols, eps,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int qwen_b200_swiglu_forward(const void *x, const void *w_gate, const void *w_up,
+                             const void *b_gate, const void *b_up, void *out, void *gate_cache,
+                             void *up_cache, long long rows, int hidden, int inter, void *stream) {
+  qb200_clear_error();
+  if (int rc = check_swiglu(x, w_gate, w_up, nullptr, b_gate, b_up, nullptr, rows, hidden, inter))
+    return rc;
+  if (rows == 0) return 0;
+  if (out == nullptr) return fail(13, "null pointer argument");
+  for (const void *q : {static_cast<const void *>(out), static_cast<const void *>(gate_cache),
+                        static_cast<const void *>(up_cache)})
+    if (q != nullptr && !al16(q)) return fail(14, "SwiGLU operands must be 16-byte aligned");
+  return swiglu_forward_launch(x, w_gate, w_up, b_gate, b_up, out, gate_cache, up_cache, rows,
+                               hidden, inter, static_cast<cudaStream_t>(stream));
+}
+
+long long qwen_b200_swiglu_forward_down_workspace(long long rows, int inter) {
+  if (rows < 0 || inter < 0) return 0;
+  return round256(rows * inter * 2);
+}
+
+int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void *w_up,
+                                  const void *w_down, const void *b_gate, const void *b_up,
+                                  const void *b_down, void *out, void *workspace,
+                                  long long rows, int hidden, int inter, void *stream) {
+  qb200_clear_error();
+  if (int rc = check_swiglu(x, w_gate, w_up, w_down, b_gate, b_up, b_down, rows, hidden, inter))
+    return rc;
+  if (rows == 0) return 0;
+  if (w_down == nullptr || out == nullptr || workspace == nullptr)
+    return fail(13, "null pointer argument");
+  if (!al16(out) || !al16(workspace)) return fail(14, "SwiGLU operands must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = swiglu_forward_launch(x, w_gate, w_up, b_gate, b_up, workspace, nullptr, nullptr,
+                                     rows, hidden, inter, st))
+    return rc;
+  return down_launch(workspace, w_down, b_down, out, rows, hidden, inter, st);
+}
+
+long long qwen_b200_rmsnorm_swiglu_down_workspace(long long rows, int hidden, int inter) {
+  if (rows < 0 || hidden < 0 || inter < 0) return 0;
+  return round256(rows * hidden * 2) + round256(rows * inter * 2);
+}
+
+int qwen_b200_rmsnorm_swiglu_down(const void *x, const void *norm_weight, void *residual,
+                                  float eps, const void *w_gate, const void *w_up,
+                                  const void *w_down, const void *b_gate, const void *b_up,
+                                  const void *b_down, void *normed, float *rms, void *out,
+                                  void *workspace, long long rows, int hidden, int inter,
+                                  void *stream) {
+  qb200_clear_error();
+  if (int rc = check_swiglu(x, w_gate, w_up, w_down, b_gate, b_up, b_down, rows, hidden, inter))
+    return rc;
+  if (rows == 0) return 0;
+  if (norm_weight == nullptr || w_down == nullptr || rms == nullptr || out == nullptr ||
+      workspace == nullptr)
+    return fail(13, "null pointer argument");
+  for (const void *q : {norm_weight, static_cast<const void *>(residual),
+                        static_cast<const void *>(normed), static_cast<const void *>(out),
+                        static_cast<const void *>(workspace)})
+    if (q != nullptr && !al16(q)) return fail(14, "operands must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  void *nbuf = normed != nullptr ? normed : ws;
+  void *sbuf = ws + round256(rows * hidden * 2);
+  if (int rc = rmsnorm_launch(nbuf, rms, x, norm_weight, residual, rows, hidden, eps, st)) return rc;
+  if (int rc = swiglu_forward_launch(nbuf, w_gate, w_up, b_gate, b_up, sbuf, nullptr, nullptr, rows,
+                                     hidden, inter, st))
+    return rc;
+  return down_launch(sbuf, w_down, b_down, out, rows, hidden, inter, st);
+}
+
+int qwen_b200_ops_status(uint64_t *detail) {
+  unsigned long long v = 0;
+  int rc = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(&v, g_ops_err, sizeof(v)) != cudaSuccess) {
+    rc = -2;
+  } else if (v != 0) {
+    rc = static_cast<int>(v >> 32);
+    const unsigned long long zero = 0;
+    cudaMemcpyToSymbol(g_ops_err, &zero, sizeof(zero));
+  }
+  if (detail) *detail = v;
+  return rc;
+}
+
+}  // extern "C"

@@ -67,3 +67,51 @@ def _call_decode(lib, num_layers=28, position=0, max_seq=2048, token=1):
 def test_launcher_rejects_bad_arguments(kw, pattern):
     rc, msg = _call_decode(ctypes.CDLL(LIB), **kw)
     assert rc != 0 and pattern in msg, (rc, msg)
+
+
+def _ops_lib():
+    lib = ctypes.CDLL(LIB)
+    vp, i, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    lib.qwen_b200_swiglu_forward.restype = i
+    lib.qwen_b200_swiglu_forward.argtypes = [vp] * 8 + [ll, i, i, vp]
+    lib.qwen_b200_rmsnorm_forward.restype = i
+    lib.qwen_b200_rmsnorm_forward.argtypes = [vp] * 5 + [ll, i, ctypes.c_float, vp]
+    lib.qwen_b200_swiglu_forward_down_workspace.restype = ll
+    lib.qwen_b200_swiglu_forward_down_workspace.argtypes = [ll, i]
+    return lib
+
+
+@pytest.mark.parametrize("rows,hidden,inter,misalign,pattern", [
+    (4, 1004, 3072, False, "multiples of 8"),
+    (4, 1024, 3070, False, "multiples of 8"),
+    (-1, 1024, 3072, False, "rows"),
+    (4, 1024, 3072, True, "16-byte aligned"),
+])
+def test_swiglu_rejects_bad_arguments(rows, hidden, inter, misalign, pattern):
+    lib = _ops_lib()
+    p = [ctypes.c_void_p(4096 * (k + 1) + (8 if misalign and k == 0 else 0)) for k in range(8)]
+    p[3] = p[4] = ctypes.c_void_p(0)  # no biases
+    rc = lib.qwen_b200_swiglu_forward(*p, rows, hidden, inter, None)
+    buf = ctypes.create_string_buffer(512)
+    assert rc != 0 and lib.qwen_b200_last_error(buf, 512) == rc
+    assert pattern in buf.value.decode(), buf.value
+
+
+def test_ops_workspace_and_empty_calls():
+    lib = _ops_lib()
+    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 3072) == 3 * 3072 * 2
+    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 40) == 256
+    # Empty inputs are a no-op (no CUDA call), even with null pointers.
+    assert lib.qwen_b200_swiglu_forward(*([None] * 8), 0, 1024, 3072, None) == 0
+    assert lib.qwen_b200_rmsnorm_forward(*([None] * 5), 0, 1024, 1e-6, None) == 0
+
+
+def test_extension_error_messages_with_numbers():
+    """An error message that formats a number must raise, not crash: the
+    extensions are built with the system C++ compiler, whose runtime matches
+    the libstdc++ torch loads."""
+    import torch
+    import swiglu_fused
+    w = torch.zeros(1024, 3072, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="got 2 dimensions"):
+        swiglu_fused.forward(torch.zeros(2, 1024, dtype=torch.float16), w, w)
