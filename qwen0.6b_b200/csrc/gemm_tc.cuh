@@ -1,0 +1,339 @@
+// gemm_tc.cuh - tcgen05 (5th-generation tensor core) GEMM for sm_100a with the
+// fused epilogues of the batched decode layer.
+//
+//   C[M, N] = A[M, K] . B[N, K]^T      A, B fp16 K-major (row-major [rows, K]),
+//                                       fp32 accumulation in tensor memory.
+//
+// One CTA computes one 128 x BN tile over the whole K range:
+//   warp 0      one lane streams A/B k-blocks (128 / BN rows x 64 halves) into a
+//               STAGES-deep shared-memory ring with TMA (128-byte swizzle, no
+//               multicast), completing on "full" mbarriers;
+//   warp 1      allocates BN tensor-memory columns, then one lane issues
+//               tcgen05.mma (M=128, N=BN, K=16) four times per k-block and
+//               frees each stage with tcgen05.commit on its "empty" mbarrier;
+//               a last commit signals the accumulator;
+//   warps 2..5  epilogue: tcgen05.ld the accumulator rows of their TMEM lane
+//               quadrant (warp % 4), apply the fused epilogue, store to global.
+// Every mbarrier wait is bounded (wall clock); a wait that gives up records a
+// status word, the roles fall through, and tensor memory is released only
+// after the last issued MMA has completed (or its own bounded wait gave up).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "ptx.cuh"
+
+namespace qb200tc {
+
+using qb200::globaltimer_ns;
+using qb200::mbar_arrive_expect_tx;
+using qb200::mbar_init;
+using qb200::mbar_try_wait;
+using qb200::smem_u32;
+
+constexpr int BM = 128;
+constexpr int BK = 64;                 // 64 halves = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;           // 6 warps
+constexpr long long WAIT_NS = 2000000000LL;
+
+enum Epilogue : int {
+  EPI_F16 = 0,         // out16[r, c] = half(acc)
+  EPI_F32 = 1,         // out32[r, c] = acc
+  EPI_F32_RES16 = 2,   // out32[r, c] = acc + float(res16[r, c])          (o_proj + residual)
+  EPI_SWIGLU = 3,      // columns (2i, 2i+1) = (gate_i, up_i):
+                       //   out16[r, i] = half(float(silu_half(half(g))) * u)
+  EPI_F16_RES32 = 4,   // out16[r, c] = half(acc + res32[r, c])            (down + residual)
+  EPI_ARGMAX = 5,      // part_val/part_idx[r, tile] = max / lowest argmax over the tile's columns
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int ldo;                      // leading dimension of the output (elements)
+  void *out;                    // fp16 or fp32 [M, ldo]
+  const void *res;              // residual (fp16 or fp32 [M, ldo]) or nullptr
+  float *part_val;              // EPI_ARGMAX: [M, n_tiles]
+  int *part_idx;
+  int n_tiles;
+  unsigned long long *err;      // status word (nullptr: none)
+};
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr size_t BYTES = static_cast<size_t>(STAGES) * STAGE + 256 + 1024;
+};
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);        // start address
+  d |= static_cast<uint64_t>(1u) << 16;                         // LBO (unused for SW128 K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;                 // SBO: next 8-row atom
+  d |= static_cast<uint64_t>(1u) << 46;                         // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                         // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M=128.
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t idesc_f16() {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __noinline__ void gemm_record(unsigned long long *err, uint32_t code) {
+  if (err == nullptr) return;
+  const unsigned long long v = (static_cast<unsigned long long>(code) << 32) |
+                               (static_cast<unsigned long long>(blockIdx.y & 0xffffu) << 16) |
+                               (blockIdx.x & 0xffffu);
+  atomicCAS(err, 0ull, v);
+}
+
+// Bounded wait; false when it gave up (or another role already did).
+__device__ __noinline__ bool gemm_wait_slow(uint64_t *bar, uint32_t parity,
+                                            volatile uint32_t *abort, unsigned long long *err,
+                                            uint32_t code) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
+      *abort = 1;
+      gemm_record(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool gemm_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
+                                          unsigned long long *err, uint32_t code) {
+  return mbar_try_wait(bar, parity) || gemm_wait_slow(bar, parity, abort, err, code);
+}
+
+// Half-precision SiLU with the upstream decode kernel's rounding steps
+// (megakernel.cu:141-154): every operation on fp16, exp2 of the fp16
+// argument evaluated in fp32 and rounded, reciprocal likewise.
+__device__ __forceinline__ __half silu_half(__half x) {
+  const __half log2e = __float2half_rn(1.44269504088896340736f);
+  const __half t = __hmul_rn(__hneg(x), log2e);
+  const __half e = __float2half_rn(exp2f(__half2float(t)));
+  const __half d = __hadd_rn(__float2half_rn(1.0f), e);
+  const __half r = __float2half_rn(1.0f / __half2float(d));
+  return __hmul_rn(x, r);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const GemmArgs g) {
+  using S = GemmSmem<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t *full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE);
+  uint64_t *empty = full + STAGES;
+  uint64_t *acc_full = empty + STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  volatile uint32_t *abort = tmem_slot + 1;
+  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (g.K + BK - 1) / BK;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort = 0;
+    qb200::fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
+        uint8_t *st = base + s * S::STAGE;
+        mbar_arrive_expect_tx(&full[s], S::STAGE);
+        tma_load_2d(st, &tm_a, kb * BK, m0, &full[s]);
+        tma_load_2d(st + S::A_BYTES, &tm_b, kb * BK, n0, &full[s]);
+        issued = kb + 1;
+      }
+      // Every issued copy lands before the CTA may exit (matters after an abort).
+      for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1))
+          if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
+            gemm_record(g.err, 4);
+            break;
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16<BN>();
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        if (!gemm_wait(&full[s], (kb / STAGES) & 1, abort, g.err, 2)) break;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(base + s * S::STAGE);
+        const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          mma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc,
+                  (kb | k) != 0 ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      // Signals the accumulator once every MMA issued above has completed
+      // (also after an abort, so tensor memory is never freed under an MMA).
+      mma_commit(acc_full);
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+    const int q = warp & 3;
+    const int row = m0 + 32 * q + lane;
+    bool ok = gemm_wait(acc_full, 0, abort, g.err, 3);
+    ok = __all_sync(0xffffffffu, ok && !*abort);  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+    if (ok) {
+      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      float best = -INFINITY;
+      int best_i = 0x7fffffff;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tq + c0, v);
+        const int col = n0 + c0;
+        if (row >= g.M || col >= g.N) continue;
+        const size_t o = static_cast<size_t>(row) * g.ldo + col;
+        const int nvalid = min(16, g.N - col);
+        if constexpr (EPI == EPI_F16) {
+          __half *out = static_cast<__half *>(g.out) + o;
+          if (nvalid == 16) {
+            uint4 pk[2];
+            __half2 *h = reinterpret_cast<__half2 *>(pk);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            reinterpret_cast<uint4 *>(out)[0] = pk[0];
+            reinterpret_cast<uint4 *>(out)[1] = pk[1];
+          } else {
+            for (int i = 0; i < nvalid; ++i) out[i] = __float2half_rn(v[i]);
+          }
+        } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RES16) {
+          float *out = static_cast<float *>(g.out) + o;
+          for (int i = 0; i < nvalid; ++i) {
+            float x = v[i];
+            if constexpr (EPI == EPI_F32_RES16)
+              x = __fadd_rn(x, __half2float(static_cast<const __half *>(g.res)[o + i]));
+            out[i] = x;
+          }
+        } else if constexpr (EPI == EPI_F16_RES32) {
+          __half *out = static_cast<__half *>(g.out) + o;
+          const float *res = static_cast<const float *>(g.res) + o;
+          for (int i = 0; i < nvalid; ++i) out[i] = __float2half_rn(__fadd_rn(v[i], res[i]));
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          // ldo counts output columns (inter); column pair (2i, 2i+1) -> output i.
+          __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
+          for (int i = 0; i + 1 < nvalid; i += 2) {
+            const float gate = v[i], up = v[i + 1];
+            const float act = __fmul_rn(__half2float(silu_half(__float2half_rn(gate))), up);
+            out[i / 2] = __float2half_rn(act);
+          }
+        } else if constexpr (EPI == EPI_ARGMAX) {
+          for (int i = 0; i < nvalid; ++i)
+            if (v[i] > best) {
+              best = v[i];
+              best_i = col + i;
+            }
+        }
+      }
+      if constexpr (EPI == EPI_ARGMAX) {
+        if (row < g.M) {
+          g.part_val[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best;
+          g.part_idx[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best_i;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace qb200tc

@@ -356,21 +356,9 @@ EncodeTiledFn encoder() {
   return g_encode;
 }
 
-// 2-D fp16 row-major [outer, inner] tensor, box {box_inner, box_outer}, zero fill.
 int make_map(CUtensorMap *m, const void *ptr, long long inner, long long outer, int box_inner,
              int box_outer) {
-  EncodeTiledFn enc = encoder();
-  if (enc == nullptr) return fail(30, "cuTensorMapEncodeTiled is unavailable from the driver");
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(31, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-  return 0;
+  return qb200_encode_f16_2d(m, ptr, inner, outer, inner, box_inner, box_outer, 0);
 }
 
 template <bool DUAL>
@@ -473,6 +461,27 @@ int down_launch(const void *s, const void *wd, const void *bd, void *out, long l
 }
 
 }  // namespace
+
+// 2-D fp16 tensor [outer, inner] with row pitch `pitch` elements, box
+// {box_inner, box_outer}, zero fill out of bounds; swizzle128 selects the
+// 128-byte shared-memory swizzle.  0 or an error code (message recorded).
+int qb200_encode_f16_2d(CUtensorMap *m, const void *ptr, long long inner, long long outer,
+                        long long pitch, int box_inner, int box_outer, int swizzle128) {
+  EncodeTiledFn enc = encoder();
+  if (enc == nullptr) return fail(30, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         swizzle128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                    : CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(31, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return 0;
+}
 
 extern "C" {
 
