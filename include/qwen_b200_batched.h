@@ -35,6 +35,46 @@ int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, co
                        void *workspace, int M, int N, int K, int ldo, void *stream);
 long long qwen_b200_gemm_argmax_workspace(int M, int N);
 
+/* Weights of one layer for the batched path (all fp16, 16-byte aligned):
+ * w_qkv [4096, 1024] = q_proj | k_proj | v_proj rows; w_gu [6144, 1024] with
+ * rows 2i = gate_proj[i], 2i+1 = up_proj[i]; w_o [1024, 2048] and
+ * w_down [1024, 3072] as in the checkpoint; norms [1024] / [128]. */
+typedef struct QwenBatchedLayer {
+  const void *input_norm, *w_qkv, *q_norm, *k_norm, *w_o, *post_norm, *w_gu, *w_down;
+} QwenBatchedLayer;
+
+/* Bytes of device workspace for up to max_rows rows per step. */
+long long qwen_b200_batched_workspace(int max_rows, int max_seq);
+
+/* Plans batched decode over `num_seqs` sequences: k_pool / v_pool are fp16
+ * [num_seqs][num_layers][8][max_seq][128] (the upstream per-sequence cache
+ * layout, Model/Qwen06B_architecture.py:233-237, stacked); embed is the tied
+ * embedding / lm_head [151936, 1024]; cos/sin tables [max_seq, 128] fp16.
+ * `layers` is a host array (copied).  Builds every tensor map once. */
+int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int num_layers,
+                             const void *embed, const void *final_norm, const void *cos_table,
+                             const void *sin_table, void *k_pool, void *v_pool, int num_seqs,
+                             int max_seq, int max_rows, void *workspace,
+                             long long workspace_bytes);
+
+/* One greedy step for `rows` rows (device int32 arrays): row r is sequence
+ * seq_ids[r] (distinct within a step) at position positions[r], fed token
+ * tokens_in[r]; K/V of that position are appended to its cache, the argmax
+ * token is written to tokens_out[r], and when norm_out is not NULL the final
+ * RMSNorm output (fp32 [rows, 1024], the logits tap) as well.  max_position
+ * must be >= every positions[r] and < max_seq (it sizes the attention grid).
+ * No host synchronisation and no allocation. */
+int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int *positions,
+                           const int *tokens_in, int *tokens_out, float *norm_out,
+                           int max_position, float attn_scale, void *stream);
+
+/* Synchronises the device; returns 0 if no batched kernel has recorded an
+ * error since the last call, else its code (1: a bounded wait gave up, 2: a
+ * token id outside the vocabulary, 3: a sequence id or position outside the
+ * caches; the offending row's access was skipped), and clears the record. */
+int qwen_b200_batched_status(void *handle, uint64_t *detail);
+void qwen_b200_batched_destroy(void *handle);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,197 @@
+"""Batched greedy decode of many independent sequences per GPU (B200).
+
+No upstream counterpart: upstream decodes one sequence at a time through
+``Decoder`` (``Model/Qwen06B_architecture.py:205-382``).  Each sequence keeps
+the upstream per-sequence fp16 KV-cache layout ``[layers, 8, max_seq, 128]``
+(``:233-237``); the caches of all sequences are stacked into one K and one V
+pool.  A step advances up to ``max_rows`` sequences by one token each through
+the C ABI of ``include/qwen_b200_batched.h`` (tcgen05 GEMMs for the
+projections and the lm_head, split-KV attention over each sequence's cache).
+
+torch only allocates device memory here; every kernel lives in
+``libqwen_b200.so``, and the class refuses to run without it.
+
+Multi-GPU: sequences are independent, so a job shards them across GPUs (one
+process per GPU, each with a full weight replica and its own sequences); no
+collective is involved.  ``shard_sequences`` gives the split.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+_lib = None
+
+H, IM, NQ, NKV, HD = 1024, 3072, 16, 8, 128
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("input_norm", "w_qkv", "q_norm", "k_norm", "w_o", "post_norm", "w_gu", "w_down")]
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        path = os.path.join(_PKG, "libqwen_b200.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: build it with qwen0.6b_b200/build.py")
+        L = ctypes.CDLL(path)
+        vp, i, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+        L.qwen_b200_batched_workspace.restype = ll
+        L.qwen_b200_batched_workspace.argtypes = [i, i]
+        L.qwen_b200_batched_create.restype = i
+        L.qwen_b200_batched_create.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(_Layer), i, vp, vp,
+                                               vp, vp, vp, vp, i, i, i, vp, ll]
+        L.qwen_b200_batched_step.restype = i
+        L.qwen_b200_batched_step.argtypes = [vp, i, vp, vp, vp, vp, vp, i, ctypes.c_float, vp]
+        L.qwen_b200_batched_status.restype = i
+        L.qwen_b200_batched_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
+        L.qwen_b200_batched_destroy.restype = None
+        L.qwen_b200_batched_destroy.argtypes = [vp]
+        L.qwen_b200_last_error.restype = i
+        L.qwen_b200_last_error.argtypes = [ctypes.c_char_p, i]
+        _lib = L
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc:
+        buf = ctypes.create_string_buffer(512)
+        lib().qwen_b200_last_error(buf, 512)
+        raise RuntimeError(f"{what} failed (code {rc}): {buf.value.decode()}")
+
+
+def shard_sequences(num_seqs: int, world: int, rank: int) -> range:
+    """Contiguous block of sequence indices owned by `rank` of `world`."""
+    per = (num_seqs + world - 1) // world
+    lo = min(num_seqs, rank * per)
+    return range(lo, min(num_seqs, lo + per))
+
+
+def pack_layer(lw: list) -> dict:
+    """Batched-path weights of one layer from its 11 upstream tensors
+    (LDGLayerWeight order): q|k|v rows stacked, gate/up rows interleaved."""
+    in_norm, q, k, v, q_norm, k_norm, o, post_norm, gate, up, down = lw
+    w_qkv = torch.cat([q, k, v], 0).contiguous()
+    w_gu = torch.stack([gate, up], 1).reshape(2 * gate.shape[0], gate.shape[1]).contiguous()
+    return dict(input_norm=in_norm.contiguous(), w_qkv=w_qkv, q_norm=q_norm.contiguous(),
+                k_norm=k_norm.contiguous(), w_o=o.contiguous(), post_norm=post_norm.contiguous(),
+                w_gu=w_gu, w_down=down.contiguous())
+
+
+class BatchedDecoder:
+    """Greedy decode of `num_seqs` independent sequences on one GPU.
+
+    weights: the ``load_weights`` dict (``embed_weight``, ``layer_weights``,
+    ``final_norm_weight``, ``cos_table``, ``sin_table``), any device.
+    Sequence s owns ``k_pool[s]`` / ``v_pool[s]`` (fp16 [layers, 8, max_seq, 128]).
+    """
+
+    def __init__(self, weights: dict, num_seqs: int, max_rows: int | None = None,
+                 max_seq: int = 2048, num_layers: int | None = None, device=None):
+        self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lw = weights["layer_weights"]
+        self.L = num_layers or len(lw) // 11
+        self.num_seqs = num_seqs
+        self.max_rows = max_rows or num_seqs
+        self.max_seq = max_seq
+        to = dict(device=self.dev)
+        self.embed = weights["embed_weight"].to(**to).contiguous()
+        self.final_norm = weights["final_norm_weight"].to(**to).contiguous()
+        self.cos = weights["cos_table"].to(**to).contiguous()
+        self.sin = weights["sin_table"].to(**to).contiguous()
+        self.layers = [pack_layer([t.to(**to) for t in lw[11 * l: 11 * l + 11]]) for l in range(self.L)]
+        # Positions a sequence has not reached are never read, so the pools need no clearing.
+        self.k_pool = torch.empty(num_seqs, self.L, NKV, max_seq, HD, dtype=torch.float16, **to)
+        self.v_pool = torch.empty_like(self.k_pool)
+        ws = lib().qwen_b200_batched_workspace(self.max_rows, max_seq)
+        self.workspace = torch.empty(ws, dtype=torch.uint8, **to)
+        self.tokens_out = torch.empty(self.max_rows, dtype=torch.int32, **to)
+        self.attn_scale = 1.0 / math.sqrt(HD)
+        arr = (_Layer * self.L)()
+        for l, d in enumerate(self.layers):
+            for name in _Layer._fields_:
+                setattr(arr[l], name[0], d[name[0]].data_ptr())
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.dev):
+            _check(lib().qwen_b200_batched_create(
+                ctypes.byref(h), arr, self.L, self.embed.data_ptr(), self.final_norm.data_ptr(),
+                self.cos.data_ptr(), self.sin.data_ptr(), self.k_pool.data_ptr(), self.v_pool.data_ptr(),
+                num_seqs, max_seq, self.max_rows, self.workspace.data_ptr(), ws), "batched_create")
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().qwen_b200_batched_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def step(self, seq_ids: torch.Tensor, positions: torch.Tensor, tokens: torch.Tensor,
+             max_position: int, norm_out: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+        """One greedy step of rows = len(seq_ids) sequences (device int32
+        tensors).  Returns the device int32 tensor of produced tokens.  No host
+        synchronisation."""
+        rows = int(seq_ids.numel())
+        for t in (seq_ids, positions, tokens):
+            if t.dtype != torch.int32 or t.device != self.dev or not t.is_contiguous():
+                raise ValueError("seq_ids, positions and tokens must be contiguous int32 tensors on "
+                                 f"{self.dev}")
+        out = self.tokens_out[:rows] if out is None else out
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        _check(lib().qwen_b200_batched_step(
+            self._h, rows, seq_ids.data_ptr(), positions.data_ptr(), tokens.data_ptr(),
+            out.data_ptr(), norm_out.data_ptr() if norm_out is not None else None,
+            int(max_position), self.attn_scale, ctypes.c_void_p(stream)), "batched_step")
+        return out
+
+    def status(self) -> int:
+        d = ctypes.c_uint64(0)
+        return lib().qwen_b200_batched_status(self._h, ctypes.byref(d))
+
+    def prefill(self, prompts: list[list[int]], seqs: list[int] | None = None) -> None:
+        """Teacher-forced steps over every prompt token but the last (as
+        upstream's ``Decoder.generate`` prefills, one position per step), rows
+        = the sequences whose prompt still has tokens at that position."""
+        seqs = list(range(len(prompts))) if seqs is None else seqs
+        longest = max(len(p) for p in prompts)
+        for t in range(longest - 1):
+            live = [i for i, p in enumerate(prompts) if t < len(p) - 1]
+            for c0 in range(0, len(live), self.max_rows):
+                chunk = live[c0: c0 + self.max_rows]
+                ids = torch.tensor([seqs[i] for i in chunk], dtype=torch.int32, device=self.dev)
+                pos = torch.full((len(chunk),), t, dtype=torch.int32, device=self.dev)
+                tok = torch.tensor([prompts[i][t] for i in chunk], dtype=torch.int32, device=self.dev)
+                self.step(ids, pos, tok, t)
+
+    def generate(self, prompts: list[list[int]], max_tokens: int) -> list[list[int]]:
+        """Prefill, then `max_tokens` greedy steps of all sequences (at most
+        max_rows of them); returns the generated ids per sequence."""
+        if len(prompts) > self.max_rows:
+            raise ValueError(f"{len(prompts)} sequences > max_rows={self.max_rows}")
+        self.prefill(prompts)
+        n = len(prompts)
+        ids = torch.arange(n, dtype=torch.int32, device=self.dev)
+        pos = torch.tensor([len(p) - 1 for p in prompts], dtype=torch.int32, device=self.dev)
+        tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=self.dev)
+        start_max = max(len(p) - 1 for p in prompts)
+        if start_max + max_tokens > self.max_seq:
+            raise ValueError("generation would run past max_seq")
+        outs = []
+        for s in range(max_tokens):
+            nxt = self.step(ids, pos, tok, start_max + s,
+                            out=torch.empty(n, dtype=torch.int32, device=self.dev))
+            outs.append(nxt)
+            tok = nxt
+            pos = pos + 1
+        return torch.stack(outs, 1).cpu().tolist()

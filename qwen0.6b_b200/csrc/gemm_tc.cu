@@ -126,7 +126,7 @@ int qb200_gemm_make_maps(GemmPlan *p, const void *a, const void *b, int M, int N
 }
 
 int qb200_gemm_run(const GemmPlan &p, int epi, GemmArgs g, cudaStream_t st) {
-  g.M = p.M;
+  g.M = (g.M > 0 && g.M < p.M) ? g.M : p.M;  // fewer rows than planned: the rest stay untouched
   g.N = p.N;
   g.K = p.K;
   g.n_tiles = (p.N + p.bn - 1) / p.bn;

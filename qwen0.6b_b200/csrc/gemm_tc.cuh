@@ -146,7 +146,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __noinline__ void gemm_record(unsigned long long *err, uint32_t code) {
+static __device__ __noinline__ void gemm_record(unsigned long long *err, uint32_t code) {
   if (err == nullptr) return;
   const unsigned long long v = (static_cast<unsigned long long>(code) << 32) |
                                (static_cast<unsigned long long>(blockIdx.y & 0xffffu) << 16) |
@@ -155,7 +155,7 @@ __device__ __noinline__ void gemm_record(unsigned long long *err, uint32_t code)
 }
 
 // Bounded wait; false when it gave up (or another role already did).
-__device__ __noinline__ bool gemm_wait_slow(uint64_t *bar, uint32_t parity,
+static __device__ __noinline__ bool gemm_wait_slow(uint64_t *bar, uint32_t parity,
                                             volatile uint32_t *abort, unsigned long long *err,
                                             uint32_t code) {
   const uint64_t t0 = globaltimer_ns();

@@ -17,8 +17,8 @@ int qb200_gemm_bn(int M, int N);
 // Builds the tensor maps (row pitches lda, ldb in elements).  0 or an error code.
 int qb200_gemm_make_maps(GemmPlan *p, const void *a, const void *b, int M, int N, int K, int lda,
                          int ldb);
-// Launches the GEMM with epilogue `epi` (qb200tc::Epilogue); g.M/N/K/n_tiles are
-// filled from the plan.
+// Launches the GEMM with epilogue `epi` (qb200tc::Epilogue) on the first g.M
+// rows (all planned rows when g.M is 0); g.N/K/n_tiles come from the plan.
 int qb200_gemm_run(const GemmPlan &p, int epi, qb200tc::GemmArgs g, cudaStream_t st);
 // out[r] = argmax over the per-tile partials of an EPI_ARGMAX GEMM.
 int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles, int rows, int *out,
