@@ -21,6 +21,12 @@ position 1920 (the KV cache of the prompt stays resident; positions
 
 Multi-GPU: single-sequence decode does not shard; ``--gpus N`` runs N
 independent replicas (one process per GPU) and reports their aggregate.
+
+``--workload batched``: 256 independent sequences per
+GPU, seeded prompt lengths uniform in [32, 512] and uniform token ids,
+prefilled with batched steps (untimed); one bench step = one batched greedy
+step of all 256 sequences (256 tokens).  Sequences are sharded per GPU (seeds
+offset by rank) with no collective; ``value`` is the aggregate tok/s.
 ``--impl reference`` times the upstream algorithm's CPU restatement (the only
 CPU implementation of this path) with all host threads, rank 0 only.
 """
@@ -175,6 +181,137 @@ def run_reference_arm(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def batched_cpu_baseline(weights_cpu: dict, pos: int, seconds: float = 10.0) -> dict:
+    """CPU oracle on one sequence at the batched workload's mean position (the
+    oracle decodes one sequence at a time; its tok/s is the CPU rate for this
+    per-token work), a bounded sample."""
+    cb = cpu_baseline(weights_cpu, seconds=seconds, start=pos)
+    cb["sample"] = "one sequence, " + cb["sample"] + f" (batched workload mean position {pos})"
+    return cb
+
+
+def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
+    """Config 4: batched greedy decode of independent sequences per GPU."""
+    from batched import BatchedDecoder
+    from qwen_weights import synthetic_weights
+
+    n = args.seqs
+    w_cpu = synthetic_weights(seed=SEED)
+    bd = BatchedDecoder(w_cpu, num_seqs=n, max_rows=n, device=dev)
+    g = torch.Generator().manual_seed(1000 + rank)
+    lengths = torch.randint(32, 513, (n,), generator=g).tolist()
+    prompts = [torch.randint(0, 151936, (ln,), generator=g).tolist() for ln in lengths]
+    bd.prefill(prompts)
+    ids = torch.arange(n, dtype=torch.int32, device=dev)
+    pos0 = torch.tensor([ln - 1 for ln in lengths], dtype=torch.int32, device=dev)
+    tok0 = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
+    start_max = max(lengths) - 1
+    total_steps = args.warmup + args.steps
+    assert start_max + 2 * total_steps < 2048
+
+    # Device-timed run: warm-up steps, then the timed steps, continuing the generation.
+    outs = [torch.empty(n, dtype=torch.int32, device=dev) for _ in range(total_steps)]
+    stream = torch.cuda.current_stream(dev)
+    pos, tok = pos0.clone(), tok0.clone()
+    for s in range(args.warmup):
+        tok = bd.step(ids, pos, tok, start_max + s, out=outs[s])
+        pos = pos + 1
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pos_list = []
+    t_start.record(stream)
+    for i in range(args.steps):
+        s = args.warmup + i
+        ev[i][0].record(stream)
+        tok = bd.step(ids, pos, tok, start_max + s, out=outs[s])
+        ev[i][1].record(stream)
+        pos_list.append(pos)
+        pos = pos + 1
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    if dist is not None:
+        dist.barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    assert bd.status() == 0, "device-side error in the batched steps"
+    ref_tokens = [o.cpu() for o in outs]
+
+    # End to end through BatchedDecoder.step: inputs from pinned host memory,
+    # tokens back to the host, every step (same positions: the cache rows are
+    # rewritten with identical values, so the tokens must repeat exactly).
+    h_in = torch.empty(3, n, dtype=torch.int32).pin_memory()
+    h_out = torch.empty(n, dtype=torch.int32).pin_memory()
+    d_in = torch.empty(3, n, dtype=torch.int32, device=dev)
+    pos, tok_h = pos0.cpu(), tok0.cpu()
+    for s in range(args.warmup):
+        pos = pos + 1
+        tok_h = ref_tokens[s]
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    h_in[0].copy_(ids.cpu())
+    for i in range(args.steps):
+        s = args.warmup + i
+        h_in[1].copy_(pos)
+        h_in[2].copy_(tok_h)
+        d_in.copy_(h_in, non_blocking=True)
+        out = bd.step(d_in[0], d_in[1], d_in[2], start_max + s)
+        h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+        tok_h = h_out.clone()
+        assert torch.equal(tok_h, ref_tokens[s]), "e2e tokens differ from the device-timed run"
+        pos = pos + 1
+    e2e_ms = 1000.0 * (time.perf_counter() - t0)
+
+    if dist is not None:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = world * n * args.steps / (total_ms / 1000.0)
+    e2e_value = world * n * args.steps / (e2e_ms / 1000.0)
+    # Algorithmic bytes per step: every weight once (layers + tied lm_head)
+    # plus the K/V of every attended position of every sequence.
+    alg = [W_BYTES + KV_BYTES_PER_POS * int((p + 1).sum()) for p in pos_list]
+    avg_alg = statistics.mean(alg)
+    avg_step_s = statistics.mean(step_ms) / 1000.0
+    peaks = measured_peaks()
+    achieved = avg_alg / avg_step_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded random-init weights, uniform-random token ids)",
+        "config": {"workload": f"config 4: batched greedy decode, {n} independent sequences per GPU, "
+                               "prompt lengths uniform in [32, 512] (prefill untimed), one step = "
+                               f"one token for each of the {n} sequences",
+                   "batch": n, "prompt_len": "uniform [32, 512]", "gen_steps": args.steps,
+                   "parallelism": f"sequence shards x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2 ({avg_alg / 1e9:.1f} GB of weights + KV read per step); no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "algorithmic_bytes_per_step": avg_alg, "avg_step_ms": avg_step_s * 1000.0},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 3 * 4 * n,
+                "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": args.steps * (28 * 9 + 3),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        mean_pos = int(statistics.mean(int(p.float().mean()) for p in pos_list))
+        line["cpu_baseline"] = batched_cpu_baseline(w_cpu, mean_pos)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    bd.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -185,6 +322,9 @@ def main() -> None:
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prefilled tokens before the timed steps (workload: 1920)")
     ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batched"],
+                    help="decode: config 2 (default); batched: config 4")
+    ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -206,6 +346,9 @@ def main() -> None:
     else:
         torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.workload == "batched":
+        run_batched(args, world, rank, local, dev, dist)
+        return
 
     from Qwen06B_architecture import Decoder
     from qwen_weights import synthetic_weights

@@ -28,11 +28,14 @@ extern "C" {
  *   4  out fp16 [M, ldo]  = half(C + res fp32 [M, ldo])
  *   5  out int32 [M]      = column of the row maximum of C (lowest on ties);
  *                           workspace of qwen_b200_gemm_argmax_workspace bytes
+ * k_splits > 1 (epilogues 0, 1, 2, 4) cuts K into that many slices computed by
+ * separate CTAs into fp32 partials (workspace of k_splits * M * N * 4 bytes),
+ * summed in slice order before the epilogue.
  * Requirements: N a multiple of 16, K a multiple of 64, 16-byte aligned
  * pointers.
  */
 int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, const void *res,
-                       void *workspace, int M, int N, int K, int ldo, void *stream);
+                       void *workspace, int M, int N, int K, int ldo, int k_splits, void *stream);
 long long qwen_b200_gemm_argmax_workspace(int M, int N);
 
 /* Weights of one layer for the batched path (all fp16, 16-byte aligned):

@@ -57,6 +57,7 @@ constexpr int CH = 128;                 // tokens per attention split
 constexpr int ATT_THREADS = 128;
 constexpr int PART = HD + 2;            // acc[128], m, l per (row, kv head, split, head)
 constexpr long long WAIT_NS = 2000000000LL;
+constexpr int KSPLIT = 4;               // split-K slices of the N=1024 GEMMs (o_proj, down)
 
 __device__ __noinline__ void record_err(unsigned long long *err, uint32_t code) {
   const unsigned long long v = (static_cast<unsigned long long>(code) << 32) |
@@ -197,7 +198,7 @@ struct AttnSmem {
   __half q[2][HD];
   float sc[2][CH];
   float red[4][2];
-  uint64_t bar;
+  uint64_t bar_k, bar_v;
   uint32_t abort;
 };
 
@@ -222,7 +223,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   const size_t seq = static_cast<size_t>(seq_id);
   const size_t base = (((seq * num_layers + layer) * NKV + g) * max_seq + t0) * HD;
   if (tid == 0) {
-    mbar_init(&sm.bar, 1);
+    mbar_init(&sm.bar_k, 1);
+    mbar_init(&sm.bar_v, 1);
     sm.abort = 0;
     qb200::fence_mbar_init();
   }
@@ -230,27 +232,30 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   if (tid == 0) {
     const uint32_t bytes = static_cast<uint32_t>(ntok) * HD * 2;
     const uint64_t pol = qb200::policy_evict_first();
-    mbar_arrive_expect_tx(&sm.bar, 2 * bytes);
-    qb200::bulk_g2s(sm.k, k_pool + base, bytes, &sm.bar, pol);
-    qb200::bulk_g2s(sm.v, v_pool + base, bytes, &sm.bar, pol);
+    mbar_arrive_expect_tx(&sm.bar_k, bytes);
+    qb200::bulk_g2s(sm.k, k_pool + base, bytes, &sm.bar_k, pol);
+    mbar_arrive_expect_tx(&sm.bar_v, bytes);
+    qb200::bulk_g2s(sm.v, v_pool + base, bytes, &sm.bar_v, pol);
   }
   {
     const __half *qs = q_rot + static_cast<size_t>(row) * QS + 2 * g * HD;
     reinterpret_cast<uint32_t *>(&sm.q[0][0])[tid] = reinterpret_cast<const uint32_t *>(qs)[tid];
   }
   __syncthreads();
-  // Wait for the copies (bounded); every thread waits so all see the data.
-  {
+  // Wait for K (bounded); every thread waits so all see the data.  V keeps
+  // landing while the scores and the softmax run.
+  auto wait_bar = [&](uint64_t *bar) {
     const uint64_t t_start = globaltimer_ns();
-    while (!mbar_try_wait(&sm.bar, 0)) {
+    while (!mbar_try_wait(bar, 0)) {
       if (static_cast<long long>(globaltimer_ns() - t_start) > WAIT_NS) {
         if (atomicExch(&sm.abort, 1u) == 0u) record_err(err, 1);
         break;
       }
     }
-  }
+  };
+  wait_bar(&sm.bar_k);
   __syncthreads();
-  const bool failed = sm.abort != 0;
+  bool failed = sm.abort != 0;
   // Scores S[h][t] = q_h . k_t on the tensor cores; A rows 0/1 = the two heads.
   uint32_t qa[8][2];
 #pragma unroll
@@ -306,6 +311,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   if (lane == 0) sm.red[warp][0] = psum;
   __syncthreads();
   const float l = sm.red[2 * hh][0] + sm.red[2 * hh + 1][0];
+  wait_bar(&sm.bar_v);
+  __syncthreads();
+  failed = sm.abort != 0;
   // P.V: thread (hh, dp) owns dims 2dp, 2dp+1 of head hh.
   const int dp = tid & 63;
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
@@ -467,7 +475,7 @@ size_t up256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
 struct Workspace {
   __half *hidden, *xn, *qkv, *qrot, *attn, *sact, *inter, *norm16;
-  float *act, *part, *arg_val;
+  float *act, *part, *arg_val, *splitk;
   int *arg_idx;
   unsigned long long *err;
 };
@@ -494,6 +502,7 @@ size_t carve(uint8_t *base, int max_rows, int max_splits, int lm_tiles, Workspac
   t.part = reinterpret_cast<float *>(take(R * NKV * max_splits * 2 * PART * 4));
   t.arg_val = reinterpret_cast<float *>(take(R * lm_tiles * 4));
   t.arg_idx = reinterpret_cast<int *>(take(R * lm_tiles * 4));
+  t.splitk = reinterpret_cast<float *>(take(KSPLIT * R * H * 4));
   t.err = reinterpret_cast<unsigned long long *>(take(64));
   if (w) *w = t;
   return off;
@@ -623,7 +632,8 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
     g.out = w.act;
     g.ldo = H;
     g.res = w.hidden;
-    if (int rc = qb200_gemm_run(p->g_o[l], qb200tc::EPI_F32_RES16, g, st)) return rc;
+    if (int rc = qb200_gemm_run_splitk(p->g_o[l], qb200tc::EPI_F32_RES16, g, KSPLIT, w.splitk, st))
+      return rc;
     post_norm_kernel<<<nb8, 256, 0, st>>>(w.act, static_cast<const __half *>(L.post_norm), w.sact, rows);
     g.out = w.inter;
     g.ldo = IM;
@@ -632,7 +642,8 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
     g.out = w.hidden;
     g.ldo = H;
     g.res = w.act;
-    if (int rc = qb200_gemm_run(p->g_down[l], qb200tc::EPI_F16_RES32, g, st)) return rc;
+    if (int rc = qb200_gemm_run_splitk(p->g_down[l], qb200tc::EPI_F16_RES32, g, KSPLIT, w.splitk, st))
+      return rc;
   }
   final_norm_kernel<<<nb8, 256, 0, st>>>(w.hidden, p->final_norm, w.norm16, norm_out, rows);
   GemmArgs g{};

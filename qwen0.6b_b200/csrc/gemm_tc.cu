@@ -46,6 +46,48 @@ __global__ void argmax_reduce_kernel(const float *__restrict__ part_val,
   if (lane == 0) out[row] = bi == 0x7fffffff ? -1 : bi;
 }
 
+// Split-K reduction: sum the k_splits fp32 partial slices in slice order and
+// apply the final epilogue.  Thread = 4 consecutive columns of one row.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ part,
+                                                            int splits, int M, int N, int epi,
+                                                            const void *__restrict__ res,
+                                                            void *__restrict__ out, int ldo) {
+  const long long q = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nq = N / 4;
+  if (q >= static_cast<long long>(M) * nq) return;
+  const int row = static_cast<int>(q / nq), col = static_cast<int>(q % nq) * 4;
+  const size_t slice = static_cast<size_t>(M) * N;
+  float4 acc = reinterpret_cast<const float4 *>(part + static_cast<size_t>(row) * N + col)[0];
+  for (int z = 1; z < splits; ++z) {
+    const float4 v = reinterpret_cast<const float4 *>(part + z * slice + static_cast<size_t>(row) * N + col)[0];
+    acc.x = __fadd_rn(acc.x, v.x);
+    acc.y = __fadd_rn(acc.y, v.y);
+    acc.z = __fadd_rn(acc.z, v.z);
+    acc.w = __fadd_rn(acc.w, v.w);
+  }
+  const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+  const size_t o = static_cast<size_t>(row) * ldo + col;
+  if (epi == EPI_F32_RES16) {
+    const __half *r = static_cast<const __half *>(res) + o;
+    float4 w;
+    w.x = __fadd_rn(a[0], __half2float(r[0]));
+    w.y = __fadd_rn(a[1], __half2float(r[1]));
+    w.z = __fadd_rn(a[2], __half2float(r[2]));
+    w.w = __fadd_rn(a[3], __half2float(r[3]));
+    *reinterpret_cast<float4 *>(static_cast<float *>(out) + o) = w;
+  } else if (epi == EPI_F16_RES32) {
+    const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(res) + o);
+    __half2 h[2] = {__floats2half2_rn(__fadd_rn(a[0], r.x), __fadd_rn(a[1], r.y)),
+                    __floats2half2_rn(__fadd_rn(a[2], r.z), __fadd_rn(a[3], r.w))};
+    *reinterpret_cast<uint2 *>(static_cast<__half *>(out) + o) = *reinterpret_cast<const uint2 *>(h);
+  } else if (epi == EPI_F32) {
+    *reinterpret_cast<float4 *>(static_cast<float *>(out) + o) = acc;
+  } else {  // EPI_F16
+    __half2 h[2] = {__floats2half2_rn(a[0], a[1]), __floats2half2_rn(a[2], a[3])};
+    *reinterpret_cast<uint2 *>(static_cast<__half *>(out) + o) = *reinterpret_cast<const uint2 *>(h);
+  }
+}
+
 }  // namespace qb200tc
 
 using namespace qb200tc;
@@ -53,7 +95,7 @@ using namespace qb200tc;
 namespace {
 
 std::mutex g_mu;
-bool g_attr[64][2][6] = {};
+bool g_attr[64][2][7] = {};
 
 int fail(int code, const char *fmt, ...) {
   char buf[512];
@@ -72,15 +114,20 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, cu
     std::lock_guard<std::mutex> lk(g_mu);
     bool &done = g_attr[dev][BN == 128][EPI];
     if (!done) {
-      const cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(GemmSmem<BN>::BYTES));
+      const cudaError_t e = cudaFuncSetAttribute(
+          gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>(GemmSmem<BN>::bytes(GemmSmem<BN>::MAX_STAGES)));
       if (e != cudaSuccess) return fail(4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       done = true;
     }
   }
-  const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM);
-  gemm_tc_kernel<BN, EPI><<<grid, THREADS, GemmSmem<BN>::BYTES, st>>>(ma, mb, g);
+  const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.k_splits > 1 ? g.k_splits : 1);
+  // One wave of CTAs: the deepest ring; more: a ring half as deep, so that
+  // two CTAs share an SM.
+  GemmArgs ga = g;
+  const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
+  ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
+  gemm_tc_kernel<BN, EPI><<<grid, THREADS, GemmSmem<BN>::bytes(ga.stages), st>>>(ma, mb, ga);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(20, "GEMM launch: %s", cudaGetErrorString(e));
   return 0;
@@ -96,6 +143,7 @@ int launch_bn(int epi, const CUtensorMap &ma, const CUtensorMap &mb, const GemmA
     case EPI_SWIGLU: return launch_t<BN, EPI_SWIGLU>(ma, mb, g, st);
     case EPI_F16_RES32: return launch_t<BN, EPI_F16_RES32>(ma, mb, g, st);
     case EPI_ARGMAX: return launch_t<BN, EPI_ARGMAX>(ma, mb, g, st);
+    case EPI_PARTIAL: return launch_t<BN, EPI_PARTIAL>(ma, mb, g, st);
     default: return fail(10, "unknown epilogue %d", epi);
   }
 }
@@ -133,6 +181,27 @@ int qb200_gemm_run(const GemmPlan &p, int epi, GemmArgs g, cudaStream_t st) {
   return p.bn == 128 ? launch_bn<128>(epi, p.ma, p.mb, g, st) : launch_bn<64>(epi, p.ma, p.mb, g, st);
 }
 
+int qb200_gemm_run_splitk(const GemmPlan &p, int epi, GemmArgs g, int splits, float *partial,
+                          cudaStream_t st) {
+  const int nk = p.K / BK;
+  if (splits < 2 || splits > nk) return fail(10, "k_splits=%d out of range [2, %d]", splits, nk);
+  if (epi != EPI_F16 && epi != EPI_F32 && epi != EPI_F32_RES16 && epi != EPI_F16_RES32)
+    return fail(10, "epilogue %d cannot follow a split-K reduction", epi);
+  GemmArgs gp = g;
+  gp.out = partial;
+  gp.ldo = p.N;
+  gp.res = nullptr;
+  gp.k_splits = splits;
+  if (int rc = qb200_gemm_run(p, EPI_PARTIAL, gp, st)) return rc;
+  const int M = (g.M > 0 && g.M < p.M) ? g.M : p.M;
+  const long long threads = static_cast<long long>(M) * (p.N / 4);
+  splitk_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
+      partial, splits, M, p.N, epi, g.res, g.out, g.ldo);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "split-K reduce launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
 int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles, int rows, int *out,
                         cudaStream_t st) {
   const int wpb = 8;
@@ -153,13 +222,14 @@ long long qwen_b200_gemm_argmax_workspace(int M, int N) {
 }
 
 int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, const void *res,
-                       void *workspace, int M, int N, int K, int ldo, void *stream) {
+                       void *workspace, int M, int N, int K, int ldo, int k_splits, void *stream) {
   qb200_clear_error();
   if (a == nullptr || b == nullptr || out == nullptr) return fail(13, "null pointer argument");
   if (epilogue < 0 || epilogue > EPI_ARGMAX) return fail(10, "unknown epilogue %d", epilogue);
   if ((epilogue == EPI_F32_RES16 || epilogue == EPI_F16_RES32) && res == nullptr)
     return fail(13, "this epilogue needs a residual");
-  if (epilogue == EPI_ARGMAX && workspace == nullptr) return fail(13, "argmax needs a workspace");
+  if ((epilogue == EPI_ARGMAX || k_splits > 1) && workspace == nullptr)
+    return fail(13, "argmax and split-K need a workspace");
   GemmPlan p{};
   if (int rc = qb200_gemm_make_maps(&p, a, b, M, N, K, K, K)) return rc;
   GemmArgs g{};
@@ -175,6 +245,7 @@ int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, co
                                          static_cast<size_t>(M) * n_tiles);
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (k_splits > 1) return qb200_gemm_run_splitk(p, epilogue, g, k_splits, static_cast<float *>(workspace), st);
   if (int rc = qb200_gemm_run(p, epilogue, g, st)) return rc;
   if (epilogue == EPI_ARGMAX)
     return qb200_argmax_reduce(g.part_val, g.part_idx, n_tiles, M, static_cast<int *>(out), st);

@@ -34,7 +34,13 @@ using qb200::smem_u32;
 
 constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 halves = one 128-byte swizzle row
-constexpr int STAGES = 4;
+// Ring depth: at most as many 24 / 32 KB stages as fit next to the barriers
+// (one CTA per SM); the launcher picks fewer (two CTAs per SM) for grids
+// larger than the GPU.
+template <int BN>
+constexpr int max_stages() {
+  return BN == 64 ? 8 : 6;
+}
 constexpr int THREADS = 192;           // 6 warps
 constexpr long long WAIT_NS = 2000000000LL;
 
@@ -46,6 +52,7 @@ enum Epilogue : int {
                        //   out16[r, i] = half(float(silu_half(half(g))) * u)
   EPI_F16_RES32 = 4,   // out16[r, c] = half(acc + res32[r, c])            (down + residual)
   EPI_ARGMAX = 5,      // part_val/part_idx[r, tile] = max / lowest argmax over the tile's columns
+  EPI_PARTIAL = 6,     // split-K: out32[z, r, c] = this CTA's partial sum over its k-range z
 };
 
 struct GemmArgs {
@@ -56,15 +63,18 @@ struct GemmArgs {
   float *part_val;              // EPI_ARGMAX: [M, n_tiles]
   int *part_idx;
   int n_tiles;
+  int k_splits;                 // grid.z: the K range is cut into this many slices (EPI_PARTIAL)
+  int stages;                   // ring depth of this launch (<= max_stages<BN>())
   unsigned long long *err;      // status word (nullptr: none)
 };
 
 template <int BN>
 struct GemmSmem {
+  static constexpr int MAX_STAGES = max_stages<BN>();
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr size_t BYTES = static_cast<size_t>(STAGES) * STAGE + 256 + 1024;
+  static constexpr size_t bytes(int stages) { return static_cast<size_t>(stages) * STAGE + 256 + 1024; }
 };
 
 // ------------------------------------------------------------------ PTX
@@ -192,17 +202,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemmArgs g) {
   using S = GemmSmem<BN>;
+  const int STAGES = g.stages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t *full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE);
-  uint64_t *empty = full + STAGES;
-  uint64_t *acc_full = empty + STAGES;
+  uint64_t *empty = full + S::MAX_STAGES;
+  uint64_t *acc_full = empty + S::MAX_STAGES;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile uint32_t *abort = tmem_slot + 1;
   constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = (g.K + BK - 1) / BK;
+  const int nk_all = (g.K + BK - 1) / BK;
+  // Split-K slice of this CTA (a single slice unless EPI_PARTIAL).
+  const int kb0 = static_cast<int>((static_cast<long long>(nk_all) * blockIdx.z) / gridDim.z);
+  const int nk = static_cast<int>((static_cast<long long>(nk_all) * (blockIdx.z + 1)) / gridDim.z) - kb0;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
 
   if (threadIdx.x == 0) {
@@ -228,8 +242,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (kb >= STAGES && !gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
         uint8_t *st = base + s * S::STAGE;
         mbar_arrive_expect_tx(&full[s], S::STAGE);
-        tma_load_2d(st, &tm_a, kb * BK, m0, &full[s]);
-        tma_load_2d(st + S::A_BYTES, &tm_b, kb * BK, n0, &full[s]);
+        tma_load_2d(st, &tm_a, (kb0 + kb) * BK, m0, &full[s]);
+        tma_load_2d(st + S::A_BYTES, &tm_b, (kb0 + kb) * BK, n0, &full[s]);
         issued = kb + 1;
       }
       // Every issued copy lands before the CTA may exit (matters after an abort).
@@ -291,6 +305,16 @@ __global__ void __launch_bounds__(THREADS, 1)
             reinterpret_cast<uint4 *>(out)[1] = pk[1];
           } else {
             for (int i = 0; i < nvalid; ++i) out[i] = __float2half_rn(v[i]);
+          }
+        } else if constexpr (EPI == EPI_PARTIAL) {
+          float *out = static_cast<float *>(g.out) +
+                       static_cast<size_t>(blockIdx.z) * g.M * g.ldo + o;
+          if (nvalid == 16) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<float4 *>(out)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          } else {
+            for (int i = 0; i < nvalid; ++i) out[i] = v[i];
           }
         } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RES16) {
           float *out = static_cast<float *>(g.out) + o;

@@ -20,6 +20,11 @@ int qb200_gemm_make_maps(GemmPlan *p, const void *a, const void *b, int M, int N
 // Launches the GEMM with epilogue `epi` (qb200tc::Epilogue) on the first g.M
 // rows (all planned rows when g.M is 0); g.N/K/n_tiles come from the plan.
 int qb200_gemm_run(const GemmPlan &p, int epi, qb200tc::GemmArgs g, cudaStream_t st);
+// Split-K: `splits` CTAs along K write fp32 partial slices into `partial`
+// ([splits, M, N]); a reduction sums them in slice order and applies `epi`
+// (EPI_F16, EPI_F32, EPI_F32_RES16 or EPI_F16_RES32) into g.out.
+int qb200_gemm_run_splitk(const GemmPlan &p, int epi, qb200tc::GemmArgs g, int splits,
+                          float *partial, cudaStream_t st);
 // out[r] = argmax over the per-tile partials of an EPI_ARGMAX GEMM.
 int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles, int rows, int *out,
                         cudaStream_t st);

@@ -23,14 +23,14 @@ def _fn():
     f = lib().qwen_b200_gemm_f16
     vp, i = ctypes.c_void_p, ctypes.c_int
     f.restype = i
-    f.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, vp]
+    f.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, i, vp]
     w = lib().qwen_b200_gemm_argmax_workspace
     w.restype = ctypes.c_longlong
     w.argtypes = [i, i]
     return f, w
 
 
-def gemm(epi, a, b, res=None, ldo=None):
+def gemm(epi, a, b, res=None, ldo=None, k_splits=1):
     f, wsz = _fn()
     M, K = a.shape
     N = b.shape[0]
@@ -42,9 +42,10 @@ def gemm(epi, a, b, res=None, ldo=None):
         out = torch.empty(M, ldo or N, dtype=torch.float32, device="cuda")
     else:
         out = torch.empty(M, ldo or N, dtype=torch.float16, device="cuda")
-    ws = torch.empty(max(16, wsz(M, N)), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(16, wsz(M, N), k_splits * M * N * 4), dtype=torch.uint8, device="cuda")
     rc = f(epi, a.data_ptr(), b.data_ptr(), out.data_ptr(), res.data_ptr() if res is not None else None,
-           ws.data_ptr(), M, N, K, ldo or N, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+           ws.data_ptr(), M, N, K, ldo or N, k_splits,
+           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     if rc:
         raise RuntimeError(last_error())
     torch.cuda.synchronize()
@@ -139,9 +140,23 @@ def test_gemm_argmax_epilogue(M, N):
     assert torch.equal(got[sel], top2.indices[sel, 0])
 
 
+@pytest.mark.parametrize("M,N,K,splits", [(256, 1024, 2048, 4), (256, 1024, 3072, 4), (77, 1024, 3072, 3),
+                                          (5, 64, 128, 2)])
+def test_gemm_split_k(M, N, K, splits):
+    a, b = _inputs(M, N, K, 17)
+    ref = ref_mm(a, b)
+    r16 = torch.randn(M, N, device="cuda").half()
+    o = gemm(EPI_F32_RES16, a, b, res=r16, k_splits=splits)
+    assert torch.allclose(o, ref + r16.float(), atol=1e-3, rtol=1e-3)
+    r32 = torch.randn(M, N, device="cuda")
+    _close16(gemm(EPI_F16_RES32, a, b, res=r32, k_splits=splits), ref + r32, "split f16+res32")
+    _close16(gemm(EPI_F16, a, b, k_splits=splits), ref, "split f16")
+    assert torch.allclose(gemm(EPI_F32, a, b, k_splits=splits), ref, atol=1e-3, rtol=1e-3)
+
+
 def test_gemm_rejects_bad_shapes():
     f, _ = _fn()
     a = torch.zeros(4, 100, dtype=torch.float16, device="cuda")
-    rc = f(EPI_F16, a.data_ptr(), a.data_ptr(), a.data_ptr(), None, None, 4, 4, 100, 4, None)
+    rc = f(EPI_F16, a.data_ptr(), a.data_ptr(), a.data_ptr(), None, None, 4, 4, 100, 4, 1, None)
     code, msg = last_error()
     assert rc != 0 and rc == code and "multiple" in msg
