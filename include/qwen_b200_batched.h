@@ -61,12 +61,16 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
                              long long workspace_bytes);
 
 /* One greedy step for `rows` rows (device int32 arrays): row r is sequence
- * seq_ids[r] (distinct within a step) at position positions[r], fed token
- * tokens_in[r]; K/V of that position are appended to its cache, the argmax
- * token is written to tokens_out[r], and when norm_out is not NULL the final
- * RMSNorm output (fp32 [rows, 1024], the logits tap) as well.  max_position
- * must be >= every positions[r] and < max_seq (it sizes the attention grid).
- * No host synchronisation and no allocation. */
+ * seq_ids[r] at position positions[r], fed token tokens_in[r]; K/V of that
+ * position are appended to its cache, the argmax token is written to
+ * tokens_out[r], and when norm_out is not NULL the final RMSNorm output
+ * (fp32 [rows, 1024], the logits tap) as well.  (sequence, position) pairs
+ * must be distinct within a step; one sequence may occupy several rows at
+ * consecutive positions (parallel prefill): every row's K/V is appended
+ * before the step's attention, so the row at position p attends to positions
+ * 0..p including those written by the same step.  max_position must be >=
+ * every positions[r] and < max_seq (it sizes the attention grid).  No host
+ * synchronisation and no allocation. */
 int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int *positions,
                            const int *tokens_in, int *tokens_out, float *norm_out,
                            int max_position, float attn_scale, void *stream);

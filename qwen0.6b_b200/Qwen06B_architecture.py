@@ -226,6 +226,26 @@ class Decoder:
     def position(self) -> int:
         return self._position
 
+    def prefill(self, token_ids: list[int], max_rows: int = 256) -> None:
+        """Parallel prefill (no upstream counterpart; upstream calls step() once
+        per prompt token, :346-347): writes the K/V of token_ids at positions
+        position .. position+len-1 with the batched tensor-core path, in steps
+        of up to max_rows tokens, and advances the position past them.  The
+        next step() / generate_nosync() continues from there."""
+        if not token_ids:
+            return
+        if self._position + len(token_ids) > MAX_SEQ_LEN:
+            raise ValueError("prefill would run past the KV cache")
+        if getattr(self, "_prefiller", None) is None or self._prefiller.max_rows != max_rows:
+            from batched import BatchedDecoder
+            self._prefiller = BatchedDecoder(
+                self._weights, num_seqs=1, max_rows=max_rows, num_layers=self._num_layers,
+                device=self._embed_weight.device, k_pool=self._k_cache.unsqueeze(0),
+                v_pool=self._v_cache.unsqueeze(0))
+        # prefill_parallel feeds all but the last token of a prompt: append one.
+        self._prefiller.prefill_parallel([list(token_ids) + [0]], starts=[self._position])
+        self._position += len(token_ids)
+
     def generate_ids(self, ids: list[int], max_tokens: int = 100, reset: bool = True) -> list[int]:
         """Prefill ids[:-1] with step(), then generate_nosync from ids[-1]."""
         if reset:

@@ -93,7 +93,8 @@ class BatchedDecoder:
     """
 
     def __init__(self, weights: dict, num_seqs: int, max_rows: int | None = None,
-                 max_seq: int = 2048, num_layers: int | None = None, device=None):
+                 max_seq: int = 2048, num_layers: int | None = None, device=None,
+                 k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None):
         self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         lw = weights["layer_weights"]
         self.L = num_layers or len(lw) // 11
@@ -107,8 +108,17 @@ class BatchedDecoder:
         self.sin = weights["sin_table"].to(**to).contiguous()
         self.layers = [pack_layer([t.to(**to) for t in lw[11 * l: 11 * l + 11]]) for l in range(self.L)]
         # Positions a sequence has not reached are never read, so the pools need no clearing.
-        self.k_pool = torch.empty(num_seqs, self.L, NKV, max_seq, HD, dtype=torch.float16, **to)
-        self.v_pool = torch.empty_like(self.k_pool)
+        # Caller-owned pools (e.g. a Decoder's own cache) must have this exact layout.
+        shape = (num_seqs, self.L, NKV, max_seq, HD)
+        if k_pool is not None or v_pool is not None:
+            for t in (k_pool, v_pool):
+                if (t is None or tuple(t.shape) != shape or t.dtype != torch.float16
+                        or not t.is_contiguous() or t.device != self.dev):
+                    raise ValueError(f"k_pool / v_pool must be contiguous fp16 {shape} on {self.dev}")
+            self.k_pool, self.v_pool = k_pool, v_pool
+        else:
+            self.k_pool = torch.empty(shape, dtype=torch.float16, **to)
+            self.v_pool = torch.empty_like(self.k_pool)
         ws = lib().qwen_b200_batched_workspace(self.max_rows, max_seq)
         self.workspace = torch.empty(ws, dtype=torch.uint8, **to)
         self.tokens_out = torch.empty(self.max_rows, dtype=torch.int32, **to)
@@ -173,6 +183,26 @@ class BatchedDecoder:
                 pos = torch.full((len(chunk),), t, dtype=torch.int32, device=self.dev)
                 tok = torch.tensor([prompts[i][t] for i in chunk], dtype=torch.int32, device=self.dev)
                 self.step(ids, pos, tok, t)
+
+    def prefill_parallel(self, prompts: list[list[int]], seqs: list[int] | None = None,
+                         starts: list[int] | None = None) -> None:
+        """Parallel prefill (no upstream counterpart; upstream feeds one prompt
+        token per step, ``Model/Qwen06B_architecture.py:346-347``): the K/V of
+        every prompt token but the last, for all sequences, in as few steps as
+        max_rows allows.  Rows of one step may be several positions of the same
+        sequence: every row's K/V is appended before the step's attention runs,
+        so the row at position p attends to the positions 0..p written by the
+        same step.  starts[i] is the position of prompts[i][0] (default 0)."""
+        seqs = list(range(len(prompts))) if seqs is None else seqs
+        starts = [0] * len(prompts) if starts is None else starts
+        rows = [(seqs[i], starts[i] + t, p[t]) for i, p in enumerate(prompts) for t in range(len(p) - 1)]
+        for c0 in range(0, len(rows), self.max_rows):
+            chunk = rows[c0: c0 + self.max_rows]
+            ids = torch.tensor([r[0] for r in chunk], dtype=torch.int32, device=self.dev)
+            pos = torch.tensor([r[1] for r in chunk], dtype=torch.int32, device=self.dev)
+            tok = torch.tensor([r[2] for r in chunk], dtype=torch.int32, device=self.dev)
+            self.step(ids, pos, tok, max(r[1] for r in chunk),
+                      out=torch.empty(len(chunk), dtype=torch.int32, device=self.dev))
 
     def generate(self, prompts: list[list[int]], max_tokens: int) -> list[list[int]]:
         """Prefill, then `max_tokens` greedy steps of all sequences (at most

@@ -145,3 +145,63 @@ def test_batched_step_rejects_bad_arguments(weights_2l):
     bad = torch.tensor([0, 7], dtype=torch.int32, device=bd.dev)
     bd.step(bad, z2, z2, 0)
     assert bd.status() == 3
+
+
+def test_parallel_prefill_matches_sequential(weights_2l):
+    """Prompt K/V written by multi-position steps (several rows of one
+    sequence per step, chunked by max_rows) equals the one-position-per-step
+    prefill within the KV tolerance, and the next step agrees."""
+    from batched import BatchedDecoder
+    prompts = _prompts([3, 100, 200], seed=12)
+    seq = BatchedDecoder(weights_2l, num_seqs=3, max_rows=3, num_layers=2)
+    par = BatchedDecoder(weights_2l, num_seqs=3, max_rows=64, num_layers=2)
+    seq.prefill(prompts)
+    par.prefill_parallel(prompts)
+    for i, p in enumerate(prompts):
+        n = len(p) - 1
+        for pool in ("k_pool", "v_pool"):
+            a, b = getattr(seq, pool)[i, :, :, :n].float(), getattr(par, pool)[i, :, :, :n].float()
+            assert float((a - b).abs().max()) <= 5e-2, f"seq {i} {pool}"
+    dev = seq.dev
+    ids = torch.arange(3, dtype=torch.int32, device=dev)
+    pos = torch.tensor([len(p) - 1 for p in prompts], dtype=torch.int32, device=dev)
+    tok = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
+    emb = seq.embed
+    outs, norms = [], []
+    for bd in (seq, par):
+        norm = torch.empty(3, 1024, dtype=torch.float32, device=dev)
+        outs.append(bd.step(ids, pos, tok, int(pos.max()), norm_out=norm,
+                            out=torch.empty(3, dtype=torch.int32, device=dev)).cpu().tolist())
+        norms.append(norm)
+    for i in range(3):
+        la, lb = logits_from_norm(norms[0][i], emb), logits_from_norm(norms[1][i], emb)
+        assert float((la - lb).abs().max()) <= LOGIT_ATOL
+        top2 = torch.topk(la, 2).values
+        if float(top2[0] - top2[1]) > MARGIN:
+            assert outs[0][i] == outs[1][i]
+
+
+def test_decoder_parallel_prefill(weights_2l):
+    """Decoder.prefill (batched path over the Decoder's own cache) then the
+    batch-1 kernel continues: same logits and tokens as step-by-step."""
+    from Qwen06B_architecture import Decoder
+    w = {k: ([t.cuda() for t in v] if isinstance(v, list) else v.cuda()) for k, v in weights_2l.items()}
+    prompt = _prompts([150], seed=13)[0]
+    a = Decoder(weights=w, verbose=False, num_layers=2)
+    b = Decoder(weights=w, verbose=False, num_layers=2)
+    for t in prompt[:-1]:
+        a.step(t)
+    b.prefill(prompt[:-1], max_rows=64)
+    assert a.position == b.position == len(prompt) - 1
+    n = len(prompt) - 1
+    assert float((a._k_cache[:, :, :n].float() - b._k_cache[:, :, :n].float()).abs().max()) <= 5e-2
+    assert float((a._v_cache[:, :, :n].float() - b._v_cache[:, :, :n].float()).abs().max()) <= 5e-2
+    ta, tb = prompt[-1], prompt[-1]
+    for s in range(4):
+        ta_next, tb_next = a.step(ta), b.step(ta)
+        la, lb = logits_from_norm(a._norm_out, w["embed_weight"]), logits_from_norm(b._norm_out, w["embed_weight"])
+        assert float((la - lb).abs().max()) <= LOGIT_ATOL, f"step {s}"
+        top2 = torch.topk(la, 2).values
+        if float(top2[0] - top2[1]) > MARGIN:
+            assert ta_next == tb_next, f"step {s}"
+        ta = ta_next
