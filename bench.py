@@ -312,6 +312,104 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
         dist.destroy_process_group()
 
 
+def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
+    """Config 5: tied lm_head + greedy argmax with the vocabulary split over the
+    ranks (one contiguous row block each), the (max, index) pairs all-gathered
+    over NCCL.  One step = the argmax of `batch` hidden rows over the whole
+    vocabulary; total work is fixed, so scaling is strong."""
+    from lmhead_shard import HIDDEN, VOCAB, ShardedLMHead
+
+    B = args.batch
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    emb = (0.02 * torch.randn(VOCAB, HIDDEN, generator=g, device=dev)).half()
+    x = torch.randn(B, HIDDEN, generator=g, device=dev).half()
+    head = ShardedLMHead(emb, world, rank, device=dev, max_rows=B)
+    del emb
+    torch.cuda.empty_cache()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        ref = head.argmax(x).clone()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        tok = head.argmax(x)
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    assert torch.equal(tok, ref), "non-deterministic sharded argmax"
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    # End to end: hidden rows from pinned host memory, tokens back to the host.
+    h_x = x.cpu().pin_memory()
+    h_tok = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_x = torch.empty_like(x)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        d_x.copy_(h_x, non_blocking=True)
+        h_tok.copy_(head.argmax(d_x), non_blocking=True)
+        stream.synchronize()
+    e2e_ms = 1000.0 * (time.perf_counter() - t0)
+    assert torch.equal(h_tok, ref.cpu())
+    if dist is not None:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = B * args.steps / (total_ms / 1000.0)
+    e2e_value = B * args.steps / (e2e_ms / 1000.0)
+    shard_bytes = (head.hi - head.lo) * HIDDEN * 2 + B * HIDDEN * 2
+    avg_step_s = statistics.mean(step_ms) / 1000.0
+    peaks = measured_peaks()
+    achieved = shard_bytes / avg_step_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,0.02) embedding, N(0,1) hidden rows)",
+        "config": {"workload": f"config 5: tied lm_head + greedy argmax of {B} hidden rows, vocabulary "
+                               f"split over {world} GPU(s), (max, index) pairs all-gathered over NCCL",
+                   "batch": B, "parallelism": f"vocab shards x{world}" if world > 1 else "single GPU",
+                   "l2": f"weights of a shard ({(head.hi - head.lo) * HIDDEN * 2 / 1e6:.1f} MB) are re-read "
+                         "each step; no flush" + (" (a shard fits in L2 at 8 GPUs)" if world >= 4 else "")},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "algorithmic_bytes_per_step": shard_bytes, "avg_step_ms": avg_step_s * 1000.0},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": B * HIDDEN * 2,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": args.steps * 3,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        e_cpu = (0.02 * torch.randn(VOCAB, HIDDEN, generator=torch.Generator().manual_seed(2))).float()
+        x_cpu = x.float().cpu()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 or n < 2:
+            (x_cpu @ e_cpu.t()).argmax(dim=1)
+            n += 1
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": B * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{n} fp32 torch matmul + argmax of {B} rows over the full "
+                                          f"vocabulary on the host ({dt:.1f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -322,8 +420,9 @@ def main() -> None:
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prefilled tokens before the timed steps (workload: 1920)")
     ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "batched"],
-                    help="decode: config 2 (default); batched: config 4")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batched", "lmhead"],
+                    help="decode: config 2 (default); batched: config 4; lmhead: config 5")
+    ap.add_argument("--batch", type=int, default=256, help="hidden rows per step (lmhead workload)")
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -348,6 +447,9 @@ def main() -> None:
     dev = torch.device("cuda", local)
     if args.workload == "batched":
         run_batched(args, world, rank, local, dev, dist)
+        return
+    if args.workload == "lmhead":
+        run_lmhead(args, world, rank, local, dev, dist)
         return
 
     from Qwen06B_architecture import Decoder

@@ -38,6 +38,26 @@ int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, co
                        void *workspace, int M, int N, int K, int ldo, int k_splits, void *stream);
 long long qwen_b200_gemm_argmax_workspace(int M, int N);
 
+/*
+ * Vocabulary-sharded tied lm_head (no upstream counterpart; upstream computes
+ * the full 151,936-row lm_head on one GPU, megakernel.cu:1001-1144).
+ * qwen_b200_lmhead_argmax: for hidden fp16 [rows, 1024] and this shard's rows
+ * of the embedding, weight fp16 [vocab_rows, 1024], writes per row the largest
+ * logit (fp32, tensor-core dot products with fp32 accumulation) and its index
+ * + index_offset (lowest among equal values).  Workspace:
+ * qwen_b200_lmhead_argmax_workspace bytes.  The dot product of one vocabulary
+ * row does not depend on the shard it sits in, so shards picked together give
+ * the single-GPU argmax exactly.
+ * qwen_b200_argmax_pick: vals / idxs [world, rows] (every shard's pair, e.g.
+ * after an all-gather) -> out[r], the largest value's index, lowest on ties.
+ */
+long long qwen_b200_lmhead_argmax_workspace(int rows, int vocab_rows);
+int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, int vocab_rows,
+                            long long index_offset, float *out_val, int *out_idx, void *workspace,
+                            void *stream);
+int qwen_b200_argmax_pick(const float *vals, const int *idxs, int world, int rows, int *out,
+                          void *stream);
+
 /* Weights of one layer for the batched path (all fp16, 16-byte aligned):
  * w_qkv [4096, 1024] = q_proj | k_proj | v_proj rows; w_gu [6144, 1024] with
  * rows 2i = gate_proj[i], 2i+1 = up_proj[i]; w_o [1024, 2048] and

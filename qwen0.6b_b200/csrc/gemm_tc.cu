@@ -88,6 +88,60 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
   }
 }
 
+// Like argmax_reduce_kernel, but keeps the winning value too and offsets the
+// index (a vocabulary shard's first row): out_val / out_idx [rows].
+__global__ void argmax_pair_kernel(const float *__restrict__ part_val,
+                                   const int *__restrict__ part_idx, int n_tiles, int rows,
+                                   long long offset, float *__restrict__ out_val,
+                                   int *__restrict__ out_idx) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int t = lane; t < n_tiles; t += 32) {
+    const float v = part_val[static_cast<size_t>(row) * n_tiles + t];
+    const int i = part_idx[static_cast<size_t>(row) * n_tiles + t];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  if (lane == 0) {
+    out_val[row] = best;
+    out_idx[row] = bi == 0x7fffffff ? -1 : static_cast<int>(bi + offset);
+  }
+}
+
+// Cross-shard pick: vals / idxs [world, rows] (one pair per shard and row) ->
+// out[r] = index of the largest value, lowest index among equal values.
+__global__ void argmax_pick_kernel(const float *__restrict__ vals, const int *__restrict__ idxs,
+                                   int world, int rows, int *__restrict__ out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float best = -INFINITY;
+  int bi = -1;
+  for (int w = 0; w < world; ++w) {
+    const float v = vals[static_cast<size_t>(w) * rows + r];
+    const int i = idxs[static_cast<size_t>(w) * rows + r];
+    if (i < 0) continue;
+    if (bi < 0 || v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  out[r] = bi;
+}
+
 }  // namespace qb200tc
 
 using namespace qb200tc;
@@ -213,6 +267,48 @@ int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles,
 }
 
 extern "C" {
+
+long long qwen_b200_lmhead_argmax_workspace(int rows, int vocab_rows) {
+  return qwen_b200_gemm_argmax_workspace(rows, vocab_rows);
+}
+
+int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, int vocab_rows,
+                            long long index_offset, float *out_val, int *out_idx, void *workspace,
+                            void *stream) {
+  qb200_clear_error();
+  if (hidden == nullptr || weight == nullptr || out_val == nullptr || out_idx == nullptr ||
+      workspace == nullptr)
+    return fail(13, "null pointer argument");
+  if (index_offset < 0 || index_offset + vocab_rows > 0x7fffffffll)
+    return fail(10, "index_offset=%lld out of range", index_offset);
+  GemmPlan p{};
+  if (int rc = qb200_gemm_make_maps(&p, hidden, weight, rows, vocab_rows, 1024, 1024, 1024)) return rc;
+  const int n_tiles = (vocab_rows + p.bn - 1) / p.bn;
+  GemmArgs g{};
+  g.ldo = 1;
+  g.part_val = static_cast<float *>(workspace);
+  g.part_idx = reinterpret_cast<int *>(g.part_val + static_cast<size_t>(rows) * n_tiles);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = qb200_gemm_run(p, EPI_ARGMAX, g, st)) return rc;
+  const int wpb = 8;
+  argmax_pair_kernel<<<(rows + wpb - 1) / wpb, 32 * wpb, 0, st>>>(g.part_val, g.part_idx, n_tiles,
+                                                                 rows, index_offset, out_val, out_idx);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "argmax launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+int qwen_b200_argmax_pick(const float *vals, const int *idxs, int world, int rows, int *out,
+                          void *stream) {
+  qb200_clear_error();
+  if (vals == nullptr || idxs == nullptr || out == nullptr) return fail(13, "null pointer argument");
+  if (world < 1 || rows < 1) return fail(10, "world=%d rows=%d out of range", world, rows);
+  argmax_pick_kernel<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(vals, idxs, world,
+                                                                                    rows, out);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "pick launch: %s", cudaGetErrorString(e));
+  return 0;
+}
 
 long long qwen_b200_gemm_argmax_workspace(int M, int N) {
   if (M < 1 || N < 16) return 0;
