@@ -196,8 +196,8 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
     from qwen_weights import synthetic_weights
 
     n = args.seqs
-    w_cpu = synthetic_weights(seed=SEED)
-    bd = BatchedDecoder(w_cpu, num_seqs=n, max_rows=n, device=dev)
+    w_cpu = synthetic_weights(seed=SEED, num_layers=args.layers)
+    bd = BatchedDecoder(w_cpu, num_seqs=n, max_rows=n, device=dev, num_layers=args.layers)
     g = torch.Generator().manual_seed(1000 + rank)
     lengths = torch.randint(32, 513, (n,), generator=g).tolist()
     prompts = [torch.randint(0, 151936, (ln,), generator=g).tolist() for ln in lengths]
@@ -225,6 +225,8 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
           for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pos_list = []
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStart()
     t_start.record(stream)
     for i in range(args.steps):
         s = args.warmup + i
@@ -235,6 +237,8 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
         pos = pos + 1
     t_end.record(stream)
     torch.cuda.synchronize(dev)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStop()
     clk = clocks.stop()
     if dist is not None:
         dist.barrier()
@@ -277,7 +281,9 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
     e2e_value = world * n * args.steps / (e2e_ms / 1000.0)
     # Algorithmic bytes per step: every weight once (layers + tied lm_head)
     # plus the K/V of every attended position of every sequence.
-    alg = [W_BYTES + KV_BYTES_PER_POS * int((p + 1).sum()) for p in pos_list]
+    w_bytes = W_BYTES if args.layers == 28 else W_BYTES - 2 * (28 - args.layers) * 15_728_640 - 2 * (28 - args.layers) * 2304
+    kv_pos = KV_BYTES_PER_POS * args.layers // 28
+    alg = [w_bytes + kv_pos * int((p + 1).sum()) for p in pos_list]
     avg_alg = statistics.mean(alg)
     avg_step_s = statistics.mean(step_ms) / 1000.0
     peaks = measured_peaks()
@@ -291,6 +297,7 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
                                "prompt lengths uniform in [32, 512] (prefill untimed), one step = "
                                f"one token for each of the {n} sequences",
                    "batch": n, "prompt_len": "uniform [32, 512]", "gen_steps": args.steps,
+                   "layers": args.layers if args.layers != 28 else None,
                    "parallelism": f"sequence shards x{world}" if world > 1 else "single GPU",
                    "l2": f"inputs larger than L2 ({avg_alg / 1e9:.1f} GB of weights + KV read per step); no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -298,7 +305,7 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
                      "algorithmic_bytes_per_step": avg_alg, "avg_step_ms": avg_step_s * 1000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 3 * 4 * n,
                 "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": args.steps * (28 * 9 + 3),
+        "gpu_launches": args.steps * (args.layers * 11 + 3),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -307,6 +314,104 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     bd.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
+    """Config 3: RMSNorm over [B, 1024] followed by the fused SwiGLU + down
+    projection (the upstream Tools/rmsnorm + Tools/swiglu forward chain, fp16
+    accumulation reproduced bit for bit).  One step = one call on B rows; 8
+    weight sets rotate so that more than the L2 capacity is in play."""
+    import swiglu_fused
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from inputs import OPS_CASE, ops_inputs
+
+    B = args.batch
+    x, w, _, wg, wu, wd = (t.to(dev) for t in ops_inputs(B))
+    sets = [(wg.clone(), wu.clone(), wd.clone()) for _ in range(8)]
+    eps = OPS_CASE["eps"]
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8])
+    ref = swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[0])[0].clone()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStart()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8])
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStop()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    h_x = x.cpu().pin_memory()
+    h_y = torch.empty(B, 1024, dtype=torch.float16).pin_memory()
+    d_x = torch.empty_like(x)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        d_x.copy_(h_x, non_blocking=True)
+        h_y.copy_(swiglu_fused.rmsnorm_forward_down(d_x, w, eps, *sets[0])[0], non_blocking=True)
+        stream.synchronize()
+    e2e_ms = 1000.0 * (time.perf_counter() - t0)
+    assert torch.equal(h_y, ref.cpu()), "non-deterministic operator output"
+    if dist is not None:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = world * B * args.steps / (total_ms / 1000.0)
+    e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
+    alg = 3 * 1024 * 3072 * 2 + 1024 * 2 + 4 * B * 1024
+    avg_step_s = statistics.mean(step_ms) / 1000.0
+    peaks = measured_peaks()
+    achieved = alg / avg_step_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (x ~ N(0,1), norm weight ~ N(1,0.1), W ~ N(0,0.02))",
+        "config": {"workload": f"config 3: RMSNorm + SwiGLU + down projection on [{B}, 1024], "
+                               "upstream fp16 accumulation order reproduced (bit-exact)",
+                   "batch": B, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "8 weight sets of 18.9 MB rotate (151 MB > L2)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "algorithmic_bytes_per_step": alg, "avg_step_ms": avg_step_s * 1000.0,
+                     "note": "the serial fp16 chains (1024 + 3072 dependent adds) bound small batches"},
+        "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": B * 2048,
+                "d2h_bytes_per_step": B * 2048},
+        "gpu_launches": args.steps * 3,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        threads = len(os.sched_getaffinity(0))
+        xs, ws_ = x.cpu(), w.cpu()
+        wgc, wuc, wdc = wg.cpu(), wu.cpu(), wd.cpu()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 or n < 1:
+            nrm, _ = O.rmsnorm_forward(xs, ws_, eps)
+            O.swiglu_forward_down(nrm.view(B, 1, 1024), wgc, wuc, wdc, nthreads=threads)
+            n += 1
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": B * n / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+                                "sample": f"{n} calls of the C restatement (same fp16 chain) on {B} rows "
+                                          f"({dt:.1f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -337,6 +442,8 @@ def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStart()
     t_start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
@@ -344,6 +451,8 @@ def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
         ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStop()
     clk = clocks.stop()
     assert torch.equal(tok, ref), "non-deterministic sharded argmax"
     total_ms = t_start.elapsed_time(t_end)
@@ -420,9 +529,13 @@ def main() -> None:
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prefilled tokens before the timed steps (workload: 1920)")
     ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "batched", "lmhead"],
-                    help="decode: config 2 (default); batched: config 4; lmhead: config 5")
-    ap.add_argument("--batch", type=int, default=256, help="hidden rows per step (lmhead workload)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "ops", "batched", "lmhead"],
+                    help="decode: config 2 (default); ops: config 3; batched: config 4; lmhead: config 5")
+    ap.add_argument("--batch", type=int, default=256, help="rows per step (ops, lmhead workloads)")
+    ap.add_argument("--layers", type=int, default=28,
+                    help="model depth of the batched workload; fewer layers only for profiling captures")
+    ap.add_argument("--profile", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -450,6 +563,9 @@ def main() -> None:
         return
     if args.workload == "lmhead":
         run_lmhead(args, world, rank, local, dev, dist)
+        return
+    if args.workload == "ops":
+        run_ops(args, world, rank, local, dev, dist)
         return
 
     from Qwen06B_architecture import Decoder
@@ -489,6 +605,8 @@ def main() -> None:
     clocks = ClockSampler(local)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStart()
     t_start.record(stream)
     outs = []
     for i in range(args.steps):
@@ -497,6 +615,8 @@ def main() -> None:
         ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
+    if args.profile:
+        torch.cuda.cudart().cudaProfilerStop()
     clk = clocks.stop()
     if dist is not None:
         dist.barrier()
