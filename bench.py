@@ -88,6 +88,7 @@ class ClockSampler:
 
     def __init__(self, gpu_index: int):
         self.proc = None
+        self.gpu = gpu_index
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -122,9 +123,25 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         if not sms:
-            return None
+            return self._one_shot()
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sms)}
+
+    def _one_shot(self) -> dict | None:
+        """A timed region shorter than the sampling interval: one reading right
+        after it (marked as such)."""
+        try:
+            out = subprocess.run(["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm,"
+                                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                                  "--format=csv,noheader,nounits", "-i", str(self.gpu)],
+                                 capture_output=True, text=True, timeout=20).stdout.strip().split(",")
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            return {"sm_mhz": float(out[0]), "sm_max_mhz": float(out[1]),
+                    "reasons": [n for n, v in zip(names, out[2:6]) if v.strip().lower() == "active"],
+                    "samples": 1, "note": "timed region shorter than the sampling interval: read right after it"}
+        except (OSError, ValueError, IndexError, subprocess.TimeoutExpired):
+            return None
 
 
 def cpu_baseline(weights_cpu: dict, seconds: float = 12.0, start: int = PROMPT_LEN) -> dict:
