@@ -192,8 +192,10 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+// K arrives as two 128-byte-swizzled halves (dims 0..63, 64..127) of CH rows
+// each (TMA tensor copies); V as one contiguous bulk copy.
 struct AttnSmem {
-  __half k[CH * HD];
+  __half k[2][CH * (HD / 2)];
   __half v[CH * HD];
   __half q[2][HD];
   float sc[2][CH];
@@ -205,8 +207,16 @@ struct AttnSmem {
 // grid (max_splits, 8 kv heads, rows), 128 threads.  Work item (row, g, j):
 // tokens [j*CH, min((j+1)*CH, pos+1)) of kv head g for q heads 2g, 2g+1;
 // writes acc[128], m, l per q head (unnormalised, fp32).
+// Offset of K[token][dim] in a 128-byte-swizzled half tile (rows of 128 B, the
+// 16-byte chunk index XORed with the row within its 8-row atom).
+__device__ __forceinline__ int k_swz(int tok, int dim) {
+  const int h = dim >> 6, d = dim & 63;
+  return h * CH * (HD / 2) + tok * (HD / 2) + ((((d >> 3) ^ (tok & 7)) << 3) | (d & 7));
+}
+
 __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
-    const __half *__restrict__ q_rot, const __half *__restrict__ k_pool,
+    const __grid_constant__ CUtensorMap tm_k, const __half *__restrict__ q_rot,
+    const __half *__restrict__ k_pool,
     const __half *__restrict__ v_pool, const int *__restrict__ seq_ids,
     const int *__restrict__ positions, float *__restrict__ part, int layer, int num_layers,
     int max_seq, int max_splits, int num_seqs, float attn_scale, unsigned long long *err) {
@@ -217,11 +227,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   const int t0 = j * CH;
   if (t0 >= n_tok || j >= max_splits) return;
   const int ntok = min(CH, n_tok - t0);
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte aligned base: the swizzled K halves need it.
+  AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t seq = static_cast<size_t>(seq_id);
-  const size_t base = (((seq * num_layers + layer) * NKV + g) * max_seq + t0) * HD;
+  const size_t krow0 = ((seq * num_layers + layer) * NKV + g) * max_seq + t0;  // row of K in the pool
+  const size_t base = krow0 * HD;
   if (tid == 0) {
     mbar_init(&sm.bar_k, 1);
     mbar_init(&sm.bar_v, 1);
@@ -232,8 +244,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   if (tid == 0) {
     const uint32_t bytes = static_cast<uint32_t>(ntok) * HD * 2;
     const uint64_t pol = qb200::policy_evict_first();
-    mbar_arrive_expect_tx(&sm.bar_k, bytes);
-    qb200::bulk_g2s(sm.k, k_pool + base, bytes, &sm.bar_k, pol);
+    // Full boxes: rows past this split's tokens are read too (masked below);
+    // rows past the end of the pool are zero-filled by the copy.
+    mbar_arrive_expect_tx(&sm.bar_k, 2 * CH * (HD / 2) * 2);
+    qb200tc::tma_load_2d(sm.k[0], &tm_k, 0, static_cast<int>(krow0), &sm.bar_k);
+    qb200tc::tma_load_2d(sm.k[1], &tm_k, HD / 2, static_cast<int>(krow0), &sm.bar_k);
     mbar_arrive_expect_tx(&sm.bar_v, bytes);
     qb200::bulk_g2s(sm.v, v_pool + base, bytes, &sm.bar_v, pol);
   }
@@ -267,13 +282,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   const int ntile = (ntok + 7) >> 3;
   if (!failed) {
     for (int tile = warp; tile < ntile; tile += 4) {
+      // Token of this lane's B column; the 8 tokens of a tile sit in different
+      // swizzle rows, so the loads below are bank-conflict free.
       const int tok = tile * 8 + (lane >> 2);
-      const __half *krow = sm.k + static_cast<size_t>(min(tok, ntok - 1)) * HD;
+      const __half *kbase = &sm.k[0][0];
       float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 2 * (lane & 3));
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 8 + 2 * (lane & 3));
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok, 16 * kk + 2 * (lane & 3)));
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok, 16 * kk + 8 + 2 * (lane & 3)));
         mma16816(d, qa[kk][0], qa[kk][1], b0, b1);
       }
       if (lane < 8) {
@@ -515,6 +532,7 @@ struct Plan {
   __half *k_pool, *v_pool;
   Workspace ws;
   GemmPlan g_qkv[64], g_o[64], g_gu[64], g_down[64], g_lm;
+  CUtensorMap tm_k;   // K pool as [num_seqs * layers * 8 * max_seq rows, 128], 64 x CH boxes, 128B swizzle
 };
 
 int lm_tiles_for(int max_rows) {
@@ -579,11 +597,14 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
     if (!rc) rc = qb200_gemm_make_maps(&p->g_down[l], p->ws.inter, L.w_down, max_rows, H, IM, IM, IM);
   }
   if (!rc) rc = qb200_gemm_make_maps(&p->g_lm, p->ws.norm16, embed, max_rows, VOCAB, H, H, H);
+  const long long k_rows = static_cast<long long>(num_seqs) * num_layers * NKV * max_seq;
+  if (!rc && k_rows > 0x7fffffffll) rc = fail(10, "KV pool of %lld rows exceeds the tensor-map range", k_rows);
+  if (!rc) rc = qb200_encode_f16_2d(&p->tm_k, k_pool, HD, k_rows, HD, HD / 2, CH, 1);
   if (rc) {
     delete p;
     return rc;
   }
-  const int smem = static_cast<int>(sizeof(AttnSmem));
+  const int smem = static_cast<int>(sizeof(AttnSmem)) + 1024;
   cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e == cudaSuccess) e = cudaMemset(p->ws.err, 0, 64);
   if (e != cudaSuccess) {
@@ -609,7 +630,7 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
   const Workspace &w = p->ws;
   const int nb8 = (rows + 7) / 8;
   const int nsplit = max_position / CH + 1;
-  const int smem = static_cast<int>(sizeof(AttnSmem));
+  const int smem = static_cast<int>(sizeof(AttnSmem)) + 1024;
   for (int l = 0; l < p->num_layers; ++l) {
     const QwenBatchedLayer &L = p->layers[l];
     input_norm_kernel<<<nb8, 256, 0, st>>>(w.hidden, l == 0 ? p->embed : nullptr, tokens_in,
@@ -626,7 +647,7 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
         p->cos_t, p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->num_layers,
         p->max_seq, p->num_seqs, w.err);
     attn_split_kernel<<<dim3(nsplit, NKV, rows), ATT_THREADS, smem, st>>>(
-        w.qrot, p->k_pool, p->v_pool, seq_ids, positions, w.part, l, p->num_layers, p->max_seq,
+        p->tm_k, w.qrot, p->k_pool, p->v_pool, seq_ids, positions, w.part, l, p->num_layers, p->max_seq,
         p->max_splits, p->num_seqs, attn_scale, w.err);
     attn_combine_kernel<<<dim3(NQ, rows), HD, 0, st>>>(w.part, positions, w.attn, p->max_splits);
     g.out = w.act;
