@@ -75,6 +75,8 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
                                                          const __half *__restrict__ w,
                                                          __half *__restrict__ xn, int rows,
                                                          unsigned long long *err) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   __half *hr = hidden + static_cast<size_t>(row) * H;
@@ -138,6 +140,8 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
     const int *__restrict__ positions, __half *__restrict__ k_pool, __half *__restrict__ v_pool,
     __half *__restrict__ q_rot, int layer, int num_layers, int max_seq, int num_seqs,
     unsigned long long *err) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = positions[row];
   const int seq_id = seq_ids[row];
@@ -220,6 +224,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
     const __half *__restrict__ v_pool, const int *__restrict__ seq_ids,
     const int *__restrict__ positions, float *__restrict__ part, int layer, int num_layers,
     int max_seq, int max_splits, int num_seqs, float attn_scale, unsigned long long *err) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int j = blockIdx.x, g = blockIdx.y, row = blockIdx.z;
   const int pos = positions[row], seq_id = seq_ids[row];
   if (seq_id < 0 || seq_id >= num_seqs || pos < 0 || pos >= max_seq) return;  // recorded by qk_rope_kv
@@ -365,6 +371,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
 __global__ void __launch_bounds__(HD) attn_combine_kernel(const float *__restrict__ part,
                                                           const int *__restrict__ positions,
                                                           __half *__restrict__ attn, int max_splits) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int qh = blockIdx.x, row = blockIdx.y, d = threadIdx.x;
   const int g = qh >> 1, h = qh & 1;
   const int ns = min(max_splits, max(0, (positions[row] + 1 + CH - 1) / CH));
@@ -389,6 +397,8 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float *__restric
 __global__ void __launch_bounds__(256) post_norm_kernel(const float *__restrict__ act,
                                                         const __half *__restrict__ w,
                                                         __half *__restrict__ sact, int rows) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const float4 *a4 = reinterpret_cast<const float4 *>(act + static_cast<size_t>(row) * H);
@@ -425,6 +435,8 @@ __global__ void __launch_bounds__(256) final_norm_kernel(const __half *__restric
                                                          const __half *__restrict__ w,
                                                          __half *__restrict__ norm16,
                                                          float *__restrict__ norm32, int rows) {
+  qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
+  qb200::griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const __half *hr = hidden + static_cast<size_t>(row) * H;
@@ -631,31 +643,43 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
   const int nb8 = (rows + 7) / 8;
   const int nsplit = max_position / CH + 1;
   const int smem = static_cast<int>(sizeof(AttnSmem)) + 1024;
+  // Every kernel of the step is launched as a programmatic dependent of the
+  // previous one (it may be scheduled while its predecessor finishes and waits
+  // for it with griddepcontrol.wait before touching its data).  The first
+  // follows whatever the caller enqueued last, which it waits for the same way.
+#define LAUNCH(kernel, grid, block, smem_bytes, ...)                                            \
+  do {                                                                                         \
+    const cudaError_t le = qb200_launch(kernel, grid, block, smem_bytes, st, true, __VA_ARGS__); \
+    if (le != cudaSuccess) return fail(20, "%s launch: %s", #kernel, cudaGetErrorString(le));   \
+  } while (0)
   for (int l = 0; l < p->num_layers; ++l) {
     const QwenBatchedLayer &L = p->layers[l];
-    input_norm_kernel<<<nb8, 256, 0, st>>>(w.hidden, l == 0 ? p->embed : nullptr, tokens_in,
-                                           static_cast<const __half *>(L.input_norm), w.xn, rows,
-                                           w.err);
+    LAUNCH(input_norm_kernel, dim3(nb8), dim3(256), 0, w.hidden, l == 0 ? p->embed : nullptr,
+           tokens_in, static_cast<const __half *>(L.input_norm), w.xn, rows, w.err);
     GemmArgs g{};
     g.M = rows;
     g.err = w.err;
+    g.pdl = 1;
     g.out = w.qkv;
     g.ldo = QKV;
     if (int rc = qb200_gemm_run(p->g_qkv[l], qb200tc::EPI_F16, g, st)) return rc;
-    qk_rope_kv_kernel<<<rows, 256, 0, st>>>(
-        w.qkv, static_cast<const __half *>(L.q_norm), static_cast<const __half *>(L.k_norm),
-        p->cos_t, p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->num_layers,
-        p->max_seq, p->num_seqs, w.err);
-    attn_split_kernel<<<dim3(nsplit, NKV, rows), ATT_THREADS, smem, st>>>(
-        p->tm_k, w.qrot, p->k_pool, p->v_pool, seq_ids, positions, w.part, l, p->num_layers, p->max_seq,
-        p->max_splits, p->num_seqs, attn_scale, w.err);
-    attn_combine_kernel<<<dim3(NQ, rows), HD, 0, st>>>(w.part, positions, w.attn, p->max_splits);
+    LAUNCH(qk_rope_kv_kernel, dim3(rows), dim3(256), 0, static_cast<const __half *>(w.qkv),
+           static_cast<const __half *>(L.q_norm), static_cast<const __half *>(L.k_norm), p->cos_t,
+           p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->num_layers, p->max_seq,
+           p->num_seqs, w.err);
+    LAUNCH(attn_split_kernel, dim3(nsplit, NKV, rows), dim3(ATT_THREADS), smem, p->tm_k,
+           static_cast<const __half *>(w.qrot), static_cast<const __half *>(p->k_pool),
+           static_cast<const __half *>(p->v_pool), seq_ids, positions, w.part, l, p->num_layers,
+           p->max_seq, p->max_splits, p->num_seqs, attn_scale, w.err);
+    LAUNCH(attn_combine_kernel, dim3(NQ, rows), dim3(HD), 0, static_cast<const float *>(w.part),
+           positions, w.attn, p->max_splits);
     g.out = w.act;
     g.ldo = H;
     g.res = w.hidden;
     if (int rc = qb200_gemm_run_splitk(p->g_o[l], qb200tc::EPI_F32_RES16, g, KSPLIT, w.splitk, st))
       return rc;
-    post_norm_kernel<<<nb8, 256, 0, st>>>(w.act, static_cast<const __half *>(L.post_norm), w.sact, rows);
+    LAUNCH(post_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const float *>(w.act),
+           static_cast<const __half *>(L.post_norm), w.sact, rows);
     g.out = w.inter;
     g.ldo = IM;
     g.res = nullptr;
@@ -666,16 +690,20 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
     if (int rc = qb200_gemm_run_splitk(p->g_down[l], qb200tc::EPI_F16_RES32, g, KSPLIT, w.splitk, st))
       return rc;
   }
-  final_norm_kernel<<<nb8, 256, 0, st>>>(w.hidden, p->final_norm, w.norm16, norm_out, rows);
+  LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const __half *>(w.hidden),
+         p->final_norm, w.norm16, norm_out, rows);
+#undef LAUNCH
   GemmArgs g{};
   g.M = rows;
   g.err = w.err;
+  g.pdl = 1;
   g.out = nullptr;
   g.ldo = 1;
   g.part_val = w.arg_val;
   g.part_idx = w.arg_idx;
   if (int rc = qb200_gemm_run(p->g_lm, qb200tc::EPI_ARGMAX, g, st)) return rc;
-  if (int rc = qb200_argmax_reduce(w.arg_val, w.arg_idx, p->lm_tiles, rows, tokens_out, st)) return rc;
+  if (int rc = qb200_argmax_reduce(w.arg_val, w.arg_idx, p->lm_tiles, rows, tokens_out, st, true))
+    return rc;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(20, "batched step launch: %s", cudaGetErrorString(e));
   return 0;

@@ -21,6 +21,8 @@ namespace qb200tc {
 __global__ void argmax_reduce_kernel(const float *__restrict__ part_val,
                                      const int *__restrict__ part_idx, int n_tiles, int rows,
                                      int *__restrict__ out) {
+  qb200::griddep_wait();
+  qb200::griddep_launch_dependents();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -52,6 +54,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
                                                             int splits, int M, int N, int epi,
                                                             const void *__restrict__ res,
                                                             void *__restrict__ out, int ldo) {
+  qb200::griddep_wait();
+  qb200::griddep_launch_dependents();
   const long long q = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nq = N / 4;
   if (q >= static_cast<long long>(M) * nq) return;
@@ -181,8 +185,8 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, cu
   GemmArgs ga = g;
   const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
   ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
-  gemm_tc_kernel<BN, EPI><<<grid, THREADS, GemmSmem<BN>::bytes(ga.stages), st>>>(ma, mb, ga);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = qb200_launch(gemm_tc_kernel<BN, EPI>, grid, dim3(THREADS),
+                                     GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0, ma, mb, ga);
   if (e != cudaSuccess) return fail(20, "GEMM launch: %s", cudaGetErrorString(e));
   return 0;
 }
@@ -249,19 +253,18 @@ int qb200_gemm_run_splitk(const GemmPlan &p, int epi, GemmArgs g, int splits, fl
   if (int rc = qb200_gemm_run(p, EPI_PARTIAL, gp, st)) return rc;
   const int M = (g.M > 0 && g.M < p.M) ? g.M : p.M;
   const long long threads = static_cast<long long>(M) * (p.N / 4);
-  splitk_reduce_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(
-      partial, splits, M, p.N, epi, g.res, g.out, g.ldo);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = qb200_launch(splitk_reduce_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)),
+                                     dim3(256), 0, st, g.pdl != 0, static_cast<const float *>(partial),
+                                     splits, M, p.N, epi, g.res, g.out, g.ldo);
   if (e != cudaSuccess) return fail(20, "split-K reduce launch: %s", cudaGetErrorString(e));
   return 0;
 }
 
 int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles, int rows, int *out,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool pdl) {
   const int wpb = 8;
-  argmax_reduce_kernel<<<(rows + wpb - 1) / wpb, 32 * wpb, 0, st>>>(part_val, part_idx, n_tiles,
-                                                                   rows, out);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = qb200_launch(argmax_reduce_kernel, dim3((rows + wpb - 1) / wpb), dim3(32 * wpb), 0,
+                                     st, pdl, part_val, part_idx, n_tiles, rows, out);
   if (e != cudaSuccess) return fail(20, "argmax launch: %s", cudaGetErrorString(e));
   return 0;
 }

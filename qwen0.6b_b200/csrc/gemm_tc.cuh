@@ -65,6 +65,7 @@ struct GemmArgs {
   int n_tiles;
   int k_splits;                 // grid.z: the K range is cut into this many slices (EPI_PARTIAL)
   int stages;                   // ring depth of this launch (<= max_stages<BN>())
+  int pdl;                      // host side: launch as a programmatic dependent of the previous kernel
   unsigned long long *err;      // status word (nullptr: none)
 };
 
@@ -233,13 +234,28 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The next kernel of the stream may be scheduled now; it waits for this
+  // grid before it reads anything this grid writes.
+  if (threadIdx.x == 0) qb200::griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
+      // B (weights) does not depend on the preceding kernel: the first ring
+      // stages are armed and their weight tiles requested before the grid
+      // dependency wait; A (activations) follows it.
+      const int pre = min(STAGES, nk);
+      for (int kb = 0; kb < pre; ++kb) {
+        uint8_t *st = base + kb * S::STAGE;
+        mbar_arrive_expect_tx(&full[kb], S::STAGE);
+        tma_load_2d(st + S::A_BYTES, &tm_b, (kb0 + kb) * BK, n0, &full[kb]);
+      }
+      qb200::griddep_wait();
+      for (int kb = 0; kb < pre; ++kb)
+        tma_load_2d(base + kb * S::STAGE, &tm_a, (kb0 + kb) * BK, m0, &full[kb]);
+      int issued = pre;
+      for (int kb = pre; kb < nk; ++kb) {
         const int s = kb % STAGES;
-        if (kb >= STAGES && !gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
+        if (!gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
         uint8_t *st = base + s * S::STAGE;
         mbar_arrive_expect_tx(&full[s], S::STAGE);
         tma_load_2d(st, &tm_a, (kb0 + kb) * BK, m0, &full[s]);
@@ -276,7 +292,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(acc_full);
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.
+    // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.  Residuals and the
+    // output buffers belong to earlier kernels until the dependency wait.
+    qb200::griddep_wait();
     const int q = warp & 3;
     const int row = m0 + 32 * q + lane;
     bool ok = gemm_wait(acc_full, 0, abort, g.err, 3);

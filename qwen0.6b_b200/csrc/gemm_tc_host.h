@@ -6,6 +6,25 @@
 
 #include "gemm_tc.cuh"
 
+// Launches `kernel` on `st`; with pdl, as a programmatic dependent of the
+// stream's previous kernel (it may start before that kernel ends and must call
+// griddepcontrol.wait before touching its outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t qb200_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                         cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Tensor maps and shape of one GEMM C[M, N] = A[M, K] . B[N, K]^T.
 struct GemmPlan {
   CUtensorMap ma, mb;
@@ -27,4 +46,4 @@ int qb200_gemm_run_splitk(const GemmPlan &p, int epi, qb200tc::GemmArgs g, int s
                           float *partial, cudaStream_t st);
 // out[r] = argmax over the per-tile partials of an EPI_ARGMAX GEMM.
 int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles, int rows, int *out,
-                        cudaStream_t st);
+                        cudaStream_t st, bool pdl = false);

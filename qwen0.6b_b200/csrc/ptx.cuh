@@ -132,6 +132,16 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *p) {
   return v;
 }
 
+// Programmatic dependent launch.  griddep_wait blocks until the preceding
+// kernel in the stream has completed and its memory is visible (a no-op when
+// this kernel was not launched as a dependent); griddep_launch_dependents lets
+// the next kernel's CTAs be scheduled once every CTA of this grid has called
+// it or exited (they still wait for this grid before reading its outputs).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Consumer-only named barrier (the producer warp never joins it).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
