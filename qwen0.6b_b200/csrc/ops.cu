@@ -20,9 +20,13 @@
 //  * A and B tiles are streamed through a 4-stage shared-memory ring by TMA
 //    tensor copies (one producer lane, mbarrier completion, no multicast), so
 //    weight bytes stay in flight while the chains run;
-//  * each thread carries two adjacent output columns as one half2 chain
-//    (gate and up: two half2 chains), using the non-contracting
-//    __hmul2_rn / __hadd2_rn so products are never fused into an FMA.
+//  * each thread carries one half2 chain (two adjacent output columns; in the
+//    gate/up kernel the gate and up chains of a column pair sit on partner
+//    lanes and meet by a shuffle), using the non-contracting __hmul2_rn /
+//    __hadd2_rn so products are never fused into an FMA; per 8 steps the
+//    loads and products are issued first and only the adds form the chain;
+//  * each kernel is a programmatic dependent of the previous one: it requests
+//    its first weight tiles before waiting for the kernel whose output it reads.
 // The chain latency (reduction length x dependent fp16 add latency) bounds a
 // small-batch call; the fp16 ALU issue rate bounds a large-batch one.
 #include <cuda.h>
@@ -35,6 +39,7 @@
 #include <mutex>
 
 #include "host_err.h"
+#include "launch.h"
 #include "ptx.cuh"
 #include "qwen_b200_ops.h"
 
@@ -52,9 +57,20 @@ constexpr int RB = 16;                  // rows per tile
 constexpr int CB = 16;                  // output columns per tile
 constexpr int KC = 128;                 // reduction chunk per ring stage
 constexpr int NST = 4;                  // ring stages
-constexpr int CONS_WARPS = 4;           // RB rows x CB/2 column pairs = 128 threads
-constexpr int CONS_THREADS = CONS_WARPS * 32;
-constexpr int THREADS = CONS_THREADS + 32;  // + producer warp
+// Consumer threads: RB rows x CB/2 column pairs, each thread one half2 chain
+// (two adjacent output columns).  In the DUAL (gate/up) kernel SPLIT puts the
+// gate and up chains of a column pair on two partner threads (shortest chain
+// per thread: the latency-bound small-row case); without SPLIT one thread
+// carries both (fewer instructions: the issue-bound many-row case).  + one
+// producer warp.
+template <bool DUAL, bool SPLIT>
+constexpr int cons_threads() {
+  return RB * (CB / 2) * (DUAL && SPLIT ? 2 : 1);
+}
+template <bool DUAL, bool SPLIT>
+constexpr int chain_threads() {
+  return cons_threads<DUAL, SPLIT>() + 32;
+}
 constexpr int A_BYTES = RB * KC * 2;    // TMA box {KC, RB} of A [rows, K]
 constexpr int B_BYTES = KC * CB * 2;    // TMA box {CB, KC} of B [K, N]
 constexpr int MAX_ROW_TILES = 65535;
@@ -129,9 +145,10 @@ __device__ __forceinline__ __half silu_c10(__half x) {
   return __float2half_rn(xf / (1.0f + expf(-xf)));
 }
 
-// grid (ceil(N / CB), ceil(rows / RB)), THREADS threads, chain_smem_bytes<DUAL>().
-template <bool DUAL>
-__global__ void __launch_bounds__(THREADS)
+// grid (ceil(N / CB), ceil(rows / RB)), chain_threads<DUAL, SPLIT>() threads,
+// chain_smem_bytes<DUAL>().
+template <bool DUAL, bool SPLIT>
+__global__ void __launch_bounds__(chain_threads<DUAL, SPLIT>())
     chain_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                       const __grid_constant__ CUtensorMap tm_b0,
                       const __grid_constant__ CUtensorMap tm_b1, const ChainArgs p) {
@@ -145,25 +162,38 @@ __global__ void __launch_bounds__(THREADS)
   uint64_t *empty = full + NST;
   volatile uint32_t *abort = reinterpret_cast<volatile uint32_t *>(empty + NST);
 
+  constexpr int CONS = cons_threads<DUAL, SPLIT>();
   const int tid = threadIdx.x;
   const int nchunks = (p.K + KC - 1) / KC;
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CONS_WARPS);
+      mbar_init(&empty[s], CONS / 32);
     }
     *abort = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  if (tid == 0) qb200::griddep_launch_dependents();
 
-  if (tid >= CONS_THREADS) {
-    // Producer: one lane streams A and B chunks into the ring.
-    if (tid != CONS_THREADS) return;
-    int issued = 0;
-    for (int c = 0; c < nchunks; ++c) {
+  if (tid >= CONS) {
+    // Producer: one lane streams A and B chunks into the ring.  The weights
+    // (B) of the first stages are requested before waiting for the previous
+    // kernel of the stream, whose output A may be.
+    if (tid != CONS) return;
+    const int pre = min(NST, nchunks);
+    for (int c = 0; c < pre; ++c) {
+      uint8_t *st = base + c * SB;
+      mbar_arrive_expect_tx(&full[c], SB);
+      tma_load_2d(st + A_BYTES, &tm_b0, blockIdx.x * CB, c * KC, &full[c]);
+      if constexpr (DUAL) tma_load_2d(st + A_BYTES + B_BYTES, &tm_b1, blockIdx.x * CB, c * KC, &full[c]);
+    }
+    qb200::griddep_wait();
+    for (int c = 0; c < pre; ++c) tma_load_2d(base + c * SB, &tm_a, c * KC, blockIdx.y * RB, &full[c]);
+    int issued = pre;
+    for (int c = pre; c < nchunks; ++c) {
       const int s = c % NST;
-      if (c >= NST && !wait_bar(&empty[s], ((c / NST) - 1) & 1, abort, ERR_EMPTY_WAIT)) break;
+      if (!wait_bar(&empty[s], ((c / NST) - 1) & 1, abort, ERR_EMPTY_WAIT)) break;
       uint8_t *st = base + s * SB;
       mbar_arrive_expect_tx(&full[s], SB);
       tma_load_2d(st, &tm_a, c * KC, blockIdx.y * RB, &full[s]);
@@ -185,53 +215,79 @@ __global__ void __launch_bounds__(THREADS)
     return;
   }
 
-  // Consumers: thread = (row in tile, column pair).
+  // Consumers: thread = (row in tile, chain m, column pair); m selects gate
+  // (0) or up (1) in the DUAL kernel.  Outputs and biases belong to earlier
+  // kernels until the dependency wait.
+  qb200::griddep_wait();
   const int lane = tid & 31;
-  const int cp = tid & 7, rl = tid >> 3;
+  const int cp = tid & 7;
+  constexpr bool TWO = DUAL && !SPLIT;            // both chains on this thread
+  const int m = DUAL && SPLIT ? (tid >> 3) & 1 : 0;
+  const int rl = DUAL && SPLIT ? tid >> 4 : tid >> 3;
   const int r = blockIdx.y * RB + rl;
   const int n = blockIdx.x * CB + 2 * cp;
   const bool active = r < p.rows && n < p.N;  // N is even, so n + 1 < N too
   const __half2 zero = __float2half2_rn(0.0f);
-  __half2 acc0 = (p.init0 != nullptr && n < p.N) ? *reinterpret_cast<const __half2 *>(p.init0 + n) : zero;
-  __half2 acc1 = zero;
-  if constexpr (DUAL) {
-    if (p.init1 != nullptr && n < p.N) acc1 = *reinterpret_cast<const __half2 *>(p.init1 + n);
-  }
+  const __half *init = m == 0 ? p.init0 : p.init1;
+  __half2 acc = (init != nullptr && n < p.N) ? *reinterpret_cast<const __half2 *>(init + n) : zero;
+  __half2 acc_up = zero;  // TWO: the up chain
+  if (TWO && p.init1 != nullptr && n < p.N) acc_up = *reinterpret_cast<const __half2 *>(p.init1 + n);
   for (int c = 0; c < nchunks; ++c) {
     const int s = c % NST;
-    if (!wait_bar(&full[s], (c / NST) & 1, abort, ERR_FULL_WAIT)) return;
+    // A warp leaves together (the final shuffle needs every lane).
+    if (!__all_sync(0xffffffffu, wait_bar(&full[s], (c / NST) & 1, abort, ERR_FULL_WAIT))) return;
     const int kn = min(KC, p.K - c * KC);  // a multiple of 8
     if (active) {
       const uint8_t *st = base + s * SB;
       const __half *arow = reinterpret_cast<const __half *>(st) + rl * KC;
-      const __half2 *b0 = reinterpret_cast<const __half2 *>(st + A_BYTES) + cp;
-      const __half2 *b1 = reinterpret_cast<const __half2 *>(st + A_BYTES + B_BYTES) + cp;
+      const __half2 *bm = reinterpret_cast<const __half2 *>(st + A_BYTES + m * B_BYTES) + cp;
+      const __half2 *bu = reinterpret_cast<const __half2 *>(st + A_BYTES + B_BYTES) + cp;
 #pragma unroll 2
       for (int k = 0; k < kn; k += 8) {
+        // Loads and products of 8 steps first, then the dependent fp16 adds
+        // in ascending k: only the adds form the serial chain.
         const uint4 av = *reinterpret_cast<const uint4 *>(arow + k);
         const __half *ah = reinterpret_cast<const __half *>(&av);
+        __half2 pr[8], pu[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const __half2 x2 = __half2half2(ah[j]);
-          acc0 = __hadd2_rn(acc0, __hmul2_rn(x2, b0[(k + j) * (CB / 2)]));
-          if constexpr (DUAL) acc1 = __hadd2_rn(acc1, __hmul2_rn(x2, b1[(k + j) * (CB / 2)]));
+          pr[j] = __hmul2_rn(x2, bm[(k + j) * (CB / 2)]);
+          if constexpr (TWO) pu[j] = __hmul2_rn(x2, bu[(k + j) * (CB / 2)]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc = __hadd2_rn(acc, pr[j]);
+          if constexpr (TWO) acc_up = __hadd2_rn(acc_up, pu[j]);
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!active) return;
   const size_t o = static_cast<size_t>(r) * p.N + n;
   if constexpr (DUAL) {
-    const __half g0 = __low2half(acc0), g1 = __high2half(acc0);
-    const __half u0 = __low2half(acc1), u1 = __high2half(acc1);
-    *reinterpret_cast<__half2 *>(p.out + o) =
-        __halves2half2(__hmul_rn(silu_c10(g0), u0), __hmul_rn(silu_c10(g1), u1));
-    if (p.cache0 != nullptr) *reinterpret_cast<__half2 *>(p.cache0 + o) = acc0;
-    if (p.cache1 != nullptr) *reinterpret_cast<__half2 *>(p.cache1 + o) = acc1;
+    __half2 up = acc_up;
+    if constexpr (SPLIT) {
+      // The up chain of this (row, column pair) is lane ^ 8 of the same warp.
+      uint32_t mine = *reinterpret_cast<uint32_t *>(&acc);
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 8);
+      up = *reinterpret_cast<const __half2 *>(&other);
+    }
+    if (!active) return;
+    if (m == 0) {
+      const __half g0 = __low2half(acc), g1 = __high2half(acc);
+      const __half u0 = __low2half(up), u1 = __high2half(up);
+      *reinterpret_cast<__half2 *>(p.out + o) =
+          __halves2half2(__hmul_rn(silu_c10(g0), u0), __hmul_rn(silu_c10(g1), u1));
+      if (p.cache0 != nullptr) *reinterpret_cast<__half2 *>(p.cache0 + o) = acc;
+      if (TWO && p.cache1 != nullptr) *reinterpret_cast<__half2 *>(p.cache1 + o) = up;
+    } else if (p.cache1 != nullptr) {
+      *reinterpret_cast<__half2 *>(p.cache1 + o) = acc;
+    }
   } else {
-    *reinterpret_cast<__half2 *>(p.out + o) = acc0;
+    if (!active) return;
+    *reinterpret_cast<__half2 *>(p.out + o) = acc;
   }
 }
 
@@ -243,6 +299,8 @@ __global__ void __launch_bounds__(256)
     rmsnorm_kernel(__half *__restrict__ out, float *__restrict__ rms,
                    const __half *__restrict__ x, const __half *__restrict__ w,
                    __half *__restrict__ res, long long rows, int cols, float eps) {
+  qb200::griddep_wait();
+  qb200::griddep_launch_dependents();
   const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -330,7 +388,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
 
 std::mutex g_ops_mu;
 EncodeTiledFn g_encode = nullptr;
-bool g_attr_set[64][2] = {};
+bool g_attr_set[64][2][2] = {};
 
 int fail(int code, const char *fmt, ...) {
   char buf[512];
@@ -361,18 +419,30 @@ int make_map(CUtensorMap *m, const void *ptr, long long inner, long long outer, 
   return qb200_encode_f16_2d(m, ptr, inner, outer, inner, box_inner, box_outer, 0);
 }
 
-template <bool DUAL>
+template <bool DUAL, bool SPLIT>
 int ensure_attr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(2, "cudaGetDevice failed");
   std::lock_guard<std::mutex> lk(g_ops_mu);
-  if (!g_attr_set[dev][DUAL]) {
-    const cudaError_t e = cudaFuncSetAttribute(chain_gemm_kernel<DUAL>,
+  if (!g_attr_set[dev][DUAL][SPLIT]) {
+    const cudaError_t e = cudaFuncSetAttribute(chain_gemm_kernel<DUAL, SPLIT>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(chain_smem_bytes<DUAL>()));
     if (e != cudaSuccess) return fail(4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    g_attr_set[dev][DUAL] = true;
+    g_attr_set[dev][DUAL][SPLIT] = true;
   }
+  return 0;
+}
+
+template <bool DUAL, bool SPLIT>
+int launch_chain_t(const CUtensorMap &ma, const CUtensorMap &mb0, const CUtensorMap &mb1,
+                   const ChainArgs &args, cudaStream_t st) {
+  if (int rc = ensure_attr<DUAL, SPLIT>()) return rc;
+  const dim3 grid((args.N + CB - 1) / CB, (args.rows + RB - 1) / RB);
+  const cudaError_t e = qb200_launch(chain_gemm_kernel<DUAL, SPLIT>, grid,
+                                     dim3(chain_threads<DUAL, SPLIT>()), chain_smem_bytes<DUAL>(), st,
+                                     true, ma, mb0, mb1, args);
+  if (e != cudaSuccess) return fail(20, "SwiGLU kernel launch: %s", cudaGetErrorString(e));
   return 0;
 }
 
@@ -380,7 +450,6 @@ int ensure_attr() {
 template <bool DUAL>
 int launch_chain(const __half *a, const __half *b0, const __half *b1, const ChainArgs &args,
                  cudaStream_t st) {
-  if (int rc = ensure_attr<DUAL>()) return rc;
   CUtensorMap ma, mb0, mb1;
   if (int rc = make_map(&ma, a, args.K, args.rows, KC, RB)) return rc;
   if (int rc = make_map(&mb0, b0, args.N, args.K, CB, KC)) return rc;
@@ -389,11 +458,10 @@ int launch_chain(const __half *a, const __half *b0, const __half *b1, const Chai
   } else {
     mb1 = mb0;
   }
-  const dim3 grid((args.N + CB - 1) / CB, (args.rows + RB - 1) / RB);
-  chain_gemm_kernel<DUAL><<<grid, THREADS, chain_smem_bytes<DUAL>(), st>>>(ma, mb0, mb1, args);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(20, "SwiGLU kernel launch: %s", cudaGetErrorString(e));
-  return 0;
+  // Gate/up of a single row tile: one chain per thread (latency-bound); more
+  // rows: both chains per thread (issue-bound).
+  if (DUAL && args.rows <= RB) return launch_chain_t<DUAL, true>(ma, mb0, mb1, args, st);
+  return launch_chain_t<DUAL, false>(ma, mb0, mb1, args, st);
 }
 
 int check_swiglu(const void *x, const void *wg, const void *wu, const void *wd, const void *bg,
@@ -424,10 +492,10 @@ int rmsnorm_launch(void *out, float *rms, const void *input, const void *weight,
   }
   const long long blocks = (rows + 7) / 8;
   if (blocks > 0x7fffffffll) return fail(10, "rows=%lld too large", rows);
-  rmsnorm_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+  const cudaError_t e = qb200_launch(
+      rmsnorm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, true,
       static_cast<__half *>(out), rms, static_cast<const __half *>(input),
       static_cast<const __half *>(weight), static_cast<__half *>(residual), rows, cols, eps);
-  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(20, "RMSNorm kernel launch: %s", cudaGetErrorString(e));
   return 0;
 }
