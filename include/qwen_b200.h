@@ -139,7 +139,9 @@ void qwen_b200_set_wait_timeout_ns(long long ns);
  * fit in `bytes`.  Events per layer: stage A/B/C/D/E entry, after-wait and
  * warp-0 end at 0..14; producer issue start / cumulative stall ns / issue end
  * at 15..17; CTA-wide end of A/B/C/D/E at 18..22; cumulative ns consumer
- * thread 0 waited for ring data at 23.  Row num_layers: final norm + lm_head
+ * thread 0 waited for ring data at 23; inside stage B: first K/V pieces
+ * landed, scores done, P.V done, split partials stored, combiner's (m, l)
+ * gathered at 24..28.  Row num_layers: final norm + lm_head
  * entry, after-wait, end, argmax after-wait, end at 0..4.  Tracing adds one
  * barrier per stage.  Pass NULL to turn it off.  The buffer must outlive the
  * launches that use it. */

@@ -82,44 +82,29 @@ _decode = _require_megakernel_op("decode")
 def load_weights(model_name: str = "Qwen/Qwen3-0.6B", verbose: bool = True):
     """Weights dict + tokenizer, in the upstream layout (upstream :97-174).
 
-    ``model_name`` of the form ``"synthetic"`` or ``"synthetic:<seed>"`` gives
+    ``model_name`` is a local checkpoint directory (or safetensors file), or a
+    Hugging Face model id resolved through the local hub cache.  The tensors
+    are read by the native safetensors reader and cast to fp16 on the device
+    (``checkpoint.load_checkpoint``; upstream instantiates the transformers
+    model for this); the tokenizer is the byte-level BPE of the checkpoint's
+    ``tokenizer.json`` (``tokenizer.QwenTokenizer``), or None when the
+    checkpoint has none.  ``"synthetic"`` or ``"synthetic:<seed>"`` gives
     seeded random-init weights and no tokenizer.
     """
     if model_name.startswith("synthetic"):
         seed = int(model_name.split(":", 1)[1]) if ":" in model_name else 0
         return synthetic_weights(seed=seed, device="cuda"), None
 
-    from transformers import AutoModelForCausalLM, AutoTokenizer
+    from checkpoint import load_checkpoint, resolve_checkpoint
+    from tokenizer import QwenTokenizer
 
+    path = resolve_checkpoint(model_name)
     if verbose:
-        print(f"Loading {model_name}...")
-    model = AutoModelForCausalLM.from_pretrained(model_name, torch_dtype=torch.float16,
-                                                 device_map="cuda")
-    tokenizer = AutoTokenizer.from_pretrained(model_name)
-    state = model.state_dict()
-    cos_table, sin_table = (t.cuda() for t in rope_tables(MAX_SEQ_LEN))
-    layer_weights = []
-    for i in range(NUM_LAYERS):
-        p = f"model.layers.{i}."
-        layer_weights.extend([
-            state[p + "input_layernorm.weight"].contiguous(),
-            state[p + "self_attn.q_proj.weight"].contiguous(),
-            state[p + "self_attn.k_proj.weight"].contiguous(),
-            state[p + "self_attn.v_proj.weight"].contiguous(),
-            state[p + "self_attn.q_norm.weight"].contiguous(),
-            state[p + "self_attn.k_norm.weight"].contiguous(),
-            state[p + "self_attn.o_proj.weight"].contiguous(),
-            state[p + "post_attention_layernorm.weight"].contiguous(),
-            state[p + "mlp.gate_proj.weight"].contiguous(),
-            state[p + "mlp.up_proj.weight"].contiguous(),
-            state[p + "mlp.down_proj.weight"].contiguous(),
-        ])
-    embed_weight = state["model.embed_tokens.weight"].contiguous()
-    weights = dict(embed_weight=embed_weight, layer_weights=layer_weights,
-                   final_norm_weight=state["model.norm.weight"].contiguous(),
-                   lm_head_weight=embed_weight, cos_table=cos_table, sin_table=sin_table)
-    del model
-    torch.cuda.empty_cache()
+        print(f"Loading {model_name} from {path}...")
+    weights = load_checkpoint(path, device="cuda")
+    tok_dir = path if os.path.isdir(path) else os.path.dirname(path)
+    tokenizer = (QwenTokenizer.from_dir(tok_dir)
+                 if os.path.exists(os.path.join(tok_dir, "tokenizer.json")) else None)
     return weights, tokenizer
 
 

@@ -143,6 +143,8 @@ enum TraceEv : int {
   TR_E0, TR_E1, TR_E2, TR_P_START, TR_P_STALL, TR_P_END,
   TR_A3, TR_B3, TR_C3, TR_D3, TR_E3,   // CTA-wide stage end (after a consumer barrier)
   TR_FW,                               // cumulative ns thread 0 waited on ring data
+  TR_B_KV, TR_B_SC, TR_B_PV, TR_B_PART, TR_B_CMB,  // stage B: K/V landed, scores, P.V, partials out, (m, l) in
+  TR_E_CYC0, TR_E_CYC1, TR_E_CYC2,     // stage E SM clock (clock64): after wait, after the k loop, end
   TR_N = 32
 };
 // Row l == num_layers holds the final stages: F entry / F after its wait /
@@ -155,6 +157,10 @@ __device__ __forceinline__ unsigned long long *trace_row(const DecodeArgs &a, in
 
 __device__ __forceinline__ void trace_mark(unsigned long long *row, int ev) {
   if (row != nullptr && threadIdx.x == 0) row[ev] = globaltimer_ns();
+}
+
+__device__ __forceinline__ void trace_clock(unsigned long long *row, int ev) {
+  if (row != nullptr && threadIdx.x == 0) row[ev] = clock64();
 }
 
 struct __align__(128) Smem {
@@ -172,10 +178,11 @@ struct __align__(128) Smem {
   float wred[NCW][2];      // per-warp score max per head
   float wsum[NCW];         // per-warp softmax sum
   float pv[2][HD];         // attention output accumulators of the split
-  __half k_fresh[HD];
+  __align__(16) __half k_fresh[HD];
   float sc[2][SC_TOK + 1];
   float att_m[2], att_l[2], att_alpha[2];
   float cmb_m[2][MAX_SPLITS], cmb_l[2][MAX_SPLITS];  // split (max, sum) per head
+  float cmb_f[2][MAX_SPLITS];                        // split rescale factor exp(m_j - M) per head
   uint32_t rowaddr[MAX_TILES * 16];  // smem address of each GEMV stage row (padding rows -> row 0)
   int rowinfo[MAX_TILES * 16];       // matrix row | kind << 24
   float mred[NCW][MAX_TILES * 16];   // per-warp partial dot products
@@ -588,7 +595,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 // epi(kind, matrix_row, dot) runs on thread j for stage row j < total.
 template <int K, class Epi>
 __device__ __forceinline__ void gemv_mma(Smem &sm, uint32_t &n, int count, int total,
-                                         const __half *x, Epi epi) {
+                                         const __half *x, Epi epi, unsigned long long *tr = nullptr) {
   constexpr int KS_W = K / 16 / NCW;
   static_assert(KS_W % 2 == 0, "two accumulator chains");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -624,6 +631,7 @@ __device__ __forceinline__ void gemv_mma(Smem &sm, uint32_t &n, int count, int t
       }
     }
   }
+  trace_clock(tr, TR_E_CYC1);
   if ((lane & 3) == 0) {
 #pragma unroll
     for (int t = 0; t < MAX_TILES; ++t) {
@@ -846,13 +854,18 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
   }
   named_bar_sync(BAR_ID, NCT);
 
-  // A fragments of q (m16n8k16, rows 0/1 = the two q heads, other rows 0):
-  // lanes 0..7 hold q[lane/4][16kk + 2(lane%4) + {0,1}] and the +8 columns.
+  // A fragments of q (m16n8k16, rows 0/1 = the two q heads, other rows 0).
+  // The k order of the MMAs is a permutation of the 128 dims that matches the
+  // 16-byte K loads below: in 32-dim block b, lane (row, c = lane & 3) holds
+  // dims 32b + 8c + 4s + {0,1} (low k half) and 32b + 8c + 4s + {2,3} (high k
+  // half) for k step 2b + s.  A dot product does not depend on the order of
+  // its terms' k steps; every product is exact and sums are fp32.
   uint32_t qa[8][2];
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    qa[kk][0] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][16 * kk + 2 * (lane & 3)]) : 0u;
-    qa[kk][1] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][16 * kk + 8 + 2 * (lane & 3)]) : 0u;
+    const int dim = 32 * (kk >> 1) + 8 * (lane & 3) + 4 * (kk & 1);
+    qa[kk][0] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][dim]) : 0u;
+    qa[kk][1] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][dim + 2]) : 0u;
   }
   const int hh = tid >> 7;                       // head of this thread (softmax, P.V)
   const int dpair = tid & 63, par = (tid >> 6) & 1;  // P.V: dims 2*dpair..+1, token parity
@@ -870,6 +883,7 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     // This super-chunk's K/V pieces: warp 0 waits, the barrier publishes.
     st.fail |= !wait_pieces(sm, w, n, 2 * npair, W_B);
     named_bar_sync(BAR_ID, NCT);
+    if (sc == 0) trace_mark(tr, TR_B_KV);
     // Scores S[h][t] = q_h . k_t on the tensor cores (fp16 inputs, exact
     // products, fp32 accumulation), 8 tokens per tile, tiles over warps.
     float wmax = -INFINITY;  // lanes 0..3: head 0, lanes 4..7: head 1
@@ -882,12 +896,21 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
         const uint32_t pn = n + 2 * (tok / KV_TOK_PER_PIECE);
         krow = reinterpret_cast<const __half *>(sm.ring[pn % NSLOTS] + (tok % KV_TOK_PER_PIECE) * KV_ROW_BYTES);
       }
+      // Lane (token g, c) loads dims 32b + 8c .. +7 of its K row with one
+      // 16-byte load per block b.  Rows are 256 B apart, so odd tokens load
+      // the blocks in the order 1,0,3,2: each load then reads 4 even rows on
+      // one half of the banks and 4 odd rows on the other (no conflict).
+      const bool odd = (lane >> 2) & 1;
+      uint4 kw[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        kw[b] = *reinterpret_cast<const uint4 *>(krow + 32 * (b ^ (odd ? 1 : 0)) + 8 * (lane & 3));
       float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 2 * (lane & 3));
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(krow + 16 * kk + 8 + 2 * (lane & 3));
-        mma16816(d, qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+      for (int b = 0; b < 4; ++b) {
+        const uint4 w = odd ? kw[b ^ 1] : kw[b];
+        mma16816(d, qa[2 * b][0], 0u, qa[2 * b][1], 0u, w.x, w.y);
+        mma16816(d, qa[2 * b + 1][0], 0u, qa[2 * b + 1][1], 0u, w.z, w.w);
       }
       if (lane < 8) {
         const int t0 = tile * 8 + 2 * (lane & 3);
@@ -906,6 +929,7 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, 2));
     if (lane == 0 || lane == 4) sm.wred[warp][lane >> 2] = wmax;
     named_bar_sync(BAR_ID, NCT);
+    if (sc == 0) trace_mark(tr, TR_B_SC);
     // Softmax (expf as upstream, megakernel.cu:490-494): every thread of head
     // hh derives the same running max, turns its tokens' scores into weights.
     float cmax = -INFINITY;
@@ -975,6 +999,7 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     n += 2 * npair;
   }
   st.n = n;
+  trace_mark(tr, TR_B_PV);
   // Add the two token parities; thread (h, d) then holds output dim d of head h.
   if (par == 1) {
     sm.pv[hh][2 * dpair] = acc0;
@@ -1001,59 +1026,55 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
       ll_store(pp + d, __float_as_uint(val), ep);
       if (d < 2) ll_store(pp + HD + d, __float_as_uint(d == 0 ? m : lsum), ep);
     }
+    trace_mark(tr, TR_B_PART);
+    bool write_out = ag.S == 1 || ag.j == 0;
+    if (!(ag.S > 1 && ag.j == 0)) trace_mark(tr, TR_B_CMB);
     if (ag.S > 1 && ag.j == 0) {
-      // Combiner (split 0).  Phase 1: thread 2*jj + h (jj >= 1) fetches split
-      // jj's (m, l) for head h into shared memory.
-      if (tid < 2 * ag.S && tid >= 2) {
-        const int jj = tid >> 1, hq = tid & 1;
-        const uint64_t *pp = a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + hq) * (HD + 2);
-        uint32_t u[2];
-        st.fail |= !ll_gather<2>(w, [&](int i) { return pp + HD + i; }, ep, u, W_B);
-        sm.cmb_m[hq][jj] = __uint_as_float(u[0]);
-        sm.cmb_l[hq][jj] = __uint_as_float(u[1]);
+      // Combiner (split 0), one gather round: thread (h, d) loads acc_j[d] of
+      // every other split j (S <= MAX_SPLITS_B200); thread 2jj + hq
+      // (1 <= jj < S) also loads split jj's (m, l) of head hq.
+      constexpr int NA = MAX_SPLITS_B200 - 1;
+      uint32_t u[NA + 2];
+      const int jm = tid >> 1, hm = tid & 1;
+      const bool ml = tid >= 2 && tid < 2 * ag.S;
+      st.fail |= !ll_gather<NA + 2>(
+          w,
+          [&](int i) {
+            if (i >= NA) {
+              const int jj = ml ? jm : 1, hq = ml ? hm : h;
+              return a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + hq) * (HD + 2) + HD + (i - NA);
+            }
+            const int jj = 1 + min(i, ag.S - 2);
+            return a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + h) * (HD + 2) + d;
+          },
+          ep, u, W_B);
+      if (ml) {
+        sm.cmb_m[hm][jm] = __uint_as_float(u[NA]);
+        sm.cmb_l[hm][jm] = __uint_as_float(u[NA + 1]);
       }
       if (tid < 2) {
         sm.cmb_m[tid][0] = sm.att_m[tid];
         sm.cmb_l[tid][0] = sm.att_l[tid];
       }
-    }
-    if (ag.S > 1) named_bar_sync(BAR_ID, NCT);
-    bool write_out = ag.S == 1 || ag.j == 0;
-    if (ag.S > 1 && ag.j == 0) {
-      // Phase 2: global max, then acc = sum_j acc_j * exp(m_j - M) and
-      // l = sum_j l_j * exp(m_j - M).
-      float M = -INFINITY;
+      named_bar_sync(BAR_ID, NCT);
+      trace_mark(tr, TR_B_CMB);
+      // Rescale factors, once per (head, split): exp(m_j - M), M the max.
+      if (tid < 2 * ag.S) {
+        float M = -INFINITY;
 #pragma unroll 1
-      for (int jj = 0; jj < ag.S; ++jj) M = fmaxf(M, sm.cmb_m[h][jj]);
-      float A = 0.f, Ls = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll 1
-        for (int jj = 0; jj < ag.S; ++jj) {
-          const float mj = sm.cmb_m[h][jj];
-          const float f = mj == -INFINITY ? 0.f : expf(mj - M);
-          Ls += sm.cmb_l[h][jj] * f;
-          if (jj == 0) A += val * f;
-        }
-        // The other splits' acc words, 9 splits per round (loads of a round
-        // are issued together).
-#pragma unroll 1
-        for (int j0 = 1; j0 < ag.S; j0 += 9) {
-          uint32_t u[9];
-          const int jn = min(9, ag.S - j0);
-          st.fail |= !ll_gather<9>(
-              w,
-              [&](int i) {
-                const int jj = j0 + min(i, jn - 1);
-                return a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + jj) * 2 + h) * (HD + 2) + d;
-              },
-              ep, u, W_B);
+        for (int jj = 0; jj < ag.S; ++jj) M = fmaxf(M, sm.cmb_m[hm][jj]);
+        const float mj = sm.cmb_m[hm][jm];
+        sm.cmb_f[hm][jm] = mj == -INFINITY ? 0.f : expf(mj - M);
+      }
+      named_bar_sync(BAR_ID, NCT);
+      // acc = sum_j acc_j f_j and l = sum_j l_j f_j, splits in order.
+      float A = val * sm.cmb_f[h][0], Ls = sm.cmb_l[h][0] * sm.cmb_f[h][0];
 #pragma unroll
-          for (int q = 0; q < 9; ++q) {
-            if (q < jn) {
-              const float mj = sm.cmb_m[h][j0 + q];
-              if (mj != -INFINITY) A = fmaf(__uint_as_float(u[q]), expf(mj - M), A);
-            }
-          }
+      for (int i = 0; i < NA; ++i) {
+        if (i < ag.S - 1) {
+          const float f = sm.cmb_f[h][i + 1];
+          A = fmaf(__uint_as_float(u[i]), f, A);
+          Ls = fmaf(sm.cmb_l[h][i + 1], f, Ls);
         }
       }
       val = A;
@@ -1172,6 +1193,7 @@ __device__ __forceinline__ bool stage_e(Smem &sm, const DecodeArgs &a, const Wai
   }
   if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
   trace_mark(tr, TR_E1);
+  trace_clock(tr, TR_E_CYC0);
   gemv_mma<IM>(
       sm, st.n, np, total, sm.xb,
       [&](int, int row, float dot) {
@@ -1179,7 +1201,9 @@ __device__ __forceinline__ bool stage_e(Smem &sm, const DecodeArgs &a, const Wai
         ll_store(a.ws.hidden + row, h2u(hv), ep);
         sm.hid_own[row - o.lo] = hv;
         a.hidden[row] = hv;
-      });
+      },
+      tr);
+  trace_clock(tr, TR_E_CYC2);
   trace_mark(tr, TR_E2);
   return false;
 }
