@@ -135,13 +135,18 @@ void qwen_b200_set_wait_timeout_ns(long long ns);
 
 /* Stage timeline for profiling (no upstream counterpart).  When a device
  * buffer is registered, later decode launches write %globaltimer stamps into
- * it: u64 [cta][step][layer 0..num_layers][32] for as many leading steps as
+ * it: u64 [cta][step][layer 0..num_layers][40] for as many leading steps as
  * fit in `bytes`.  Events per layer: stage A/B/C/D/E entry, after-wait and
  * warp-0 end at 0..14; producer issue start / cumulative stall ns / issue end
  * at 15..17; CTA-wide end of A/B/C/D/E at 18..22; cumulative ns consumer
  * thread 0 waited for ring data at 23; inside stage B: first K/V pieces
  * landed, scores done, P.V done, split partials stored, combiner's (m, l)
- * gathered at 24..28.  Row num_layers: final norm + lm_head
+ * gathered at 24..28; SM clock (clock64) in stage E after its wait, after
+ * the k loop and at its end at 29..31, and in stage B after the scores, the
+ * softmax, the P.V loop and the ring release at 32..35; stage A: ring pieces
+ * landed (warp 0) and hidden words gathered (thread 0) at 36..37; producer
+ * issue of the layer's last stage-A piece at 38.  Row num_layers: final
+ * norm + lm_head
  * entry, after-wait, end, argmax after-wait, end at 0..4.  Tracing adds one
  * barrier per stage.  Pass NULL to turn it off.  The buffer must outlive the
  * launches that use it. */

@@ -53,13 +53,10 @@ constexpr int NCW = 8;                // consumer warps
 constexpr int NCT = NCW * 32;         // consumer threads
 constexpr int NTHREADS = NCT + 32;    // + one producer warp
 // A ring piece carries up to PIECE_BYTES of payload: 6 weight rows of
-// K=1024, 3 of 2048, 2 of 3072, 48 KV-cache rows or 6 lm_head rows.  Weight
-// rows of the layer GEMVs are stored with a pitch of row_bytes + 16 and a
-// piece offset of 16 * (stage row index) mod 128, so that any 8 consecutive
-// stage rows start in 8 different 16-byte bank groups (conflict-free
-// ldmatrix); the slot keeps room for that padding.
+// K=1024, 3 of 2048, 2 of 3072, 48 KV-cache rows or 6 lm_head rows, stored
+// densely (one bulk copy per piece).
 constexpr int PIECE_BYTES = 12288;
-constexpr int SLOT_BYTES = 12544;
+constexpr int SLOT_BYTES = PIECE_BYTES;
 constexpr int NSLOTS = 16;
 constexpr int BATCH_MAX = 8;          // pieces per consumer batch (<= NSLOTS/2)
 // Bulk copies in flight per CTA (issued, not yet landed).  The ring may hold
@@ -67,7 +64,7 @@ constexpr int BATCH_MAX = 8;          // pieces per consumer batch (<= NSLOTS/2)
 // latency only queue in the memory system and delay every other access on
 // the critical path (handoff words, norm weights).
 #ifndef QB200_INFLIGHT
-#define QB200_INFLIGHT 5
+#define QB200_INFLIGHT 8
 #endif
 constexpr int INFLIGHT = QB200_INFLIGHT;
 constexpr int KV_ROW_BYTES = HD * 2;
@@ -145,7 +142,10 @@ enum TraceEv : int {
   TR_FW,                               // cumulative ns thread 0 waited on ring data
   TR_B_KV, TR_B_SC, TR_B_PV, TR_B_PART, TR_B_CMB,  // stage B: K/V landed, scores, P.V, partials out, (m, l) in
   TR_E_CYC0, TR_E_CYC1, TR_E_CYC2,     // stage E SM clock (clock64): after wait, after the k loop, end
-  TR_N = 32
+  TR_B_CYC0, TR_B_CYC1, TR_B_CYC2, TR_B_CYC3,  // stage B SM clock: scores done, softmax, P.V loop, ring release
+  TR_A_PIECES, TR_A_GATHER,            // stage A: warp 0 saw all ring pieces, thread 0 gathered the hidden words
+  TR_P_A_LAST,                         // producer: issue of this layer's last stage-A piece
+  TR_N = 40
 };
 // Row l == num_layers holds the final stages: F entry / F after its wait /
 // F end / G after its wait / G end at events 0..4.
@@ -177,9 +177,9 @@ struct __align__(128) Smem {
   __half q_rot[2][HD];     // rotated q of the two heads (fp16, as upstream rounds it)
   float wred[NCW][2];      // per-warp score max per head
   float wsum[NCW];         // per-warp softmax sum
-  float pv[2][HD];         // attention output accumulators of the split
+  __align__(16) float pvp[4][2][HD];  // P.V partials of the four token slices [slice][head][dim]
   __align__(16) __half k_fresh[HD];
-  float sc[2][SC_TOK + 1];
+  __align__(16) float sc[SC_TOK + 1][2];  // scores, then softmax weights [token][head]
   float att_m[2], att_l[2], att_alpha[2];
   float cmb_m[2][MAX_SPLITS], cmb_l[2][MAX_SPLITS];  // split (max, sum) per head
   float cmb_f[2][MAX_SPLITS];                        // split rescale factor exp(m_j - M) per head
@@ -247,14 +247,18 @@ __device__ __forceinline__ bool wait_ok(const WaitCtx &w, uint64_t t0, uint32_t 
   return true;
 }
 
+// backoff: sleep between polls (the producer's wait for a free ring slot,
+// which is off the critical path; a hot poll would take issue slots from the
+// consumer warps on its SM sub-partition).
 __device__ __noinline__ bool wait_mbar_slow(WaitCtx w, uint64_t *bar, uint32_t parity,
-                                            uint32_t code, uint32_t where) {
+                                            uint32_t code, uint32_t where, bool backoff = false) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) {
       if (w.fullwait != nullptr && threadIdx.x == 0) *w.fullwait += globaltimer_ns() - t0;
       return true;
     }
+    if (backoff) __nanosleep(200);
     if ((it & 63) == 0 && !wait_ok(w, t0, code, where)) return false;
   }
 }
@@ -319,7 +323,6 @@ __device__ __forceinline__ int npieces(int nrows, int row_bytes) {
   return (nrows + rpp - 1) / rpp;
 }
 
-__device__ __forceinline__ uint32_t row_pad(int stage_row) { return (16u * stage_row) & 127u; }
 
 __device__ __forceinline__ Piece seg_piece(const void *base, int row_bytes, int row0, int nrows,
                                            int i, int kind) {
@@ -419,16 +422,17 @@ __device__ __forceinline__ WaitCtx make_wait(const DecodeArgs &a, Smem &sm) {
 }
 
 // ------------------------------------------------------------- producer
-// Issues ring piece n (one bulk copy, or one per padded weight row when
-// stage_row >= 0) after its slot was released and piece n-INFLIGHT landed.
+// Issues ring piece n (one bulk copy) after its slot was released and piece
+// n-INFLIGHT landed.  One copy per piece, never one per weight row: the copy
+// engine's per-copy cost caps a CTA at about 24 GB/s with 2 KB copies
+// against about 47 GB/s with 12 KB copies (measured on B200).
 __device__ __noinline__ bool issue_piece(Smem &sm, WaitCtx w, uint32_t n, const char *src,
-                                         uint32_t bytes, int nrows, int stage_row, uint64_t pol,
-                                         unsigned long long *stall_ns) {
+                                         uint32_t bytes, uint64_t pol, unsigned long long *stall_ns) {
   const int slot = n % NSLOTS;
   const uint32_t round = n / NSLOTS;
   if (round > 0 && !mbar_try_wait(&sm.empty[slot], (round - 1) & 1)) {
     const uint64_t t0 = stall_ns ? globaltimer_ns() : 0;
-    if (!wait_mbar_slow(w, &sm.empty[slot], (round - 1) & 1, ST_TIMEOUT_EMPTY, W_PROD)) return false;
+    if (!wait_mbar_slow(w, &sm.empty[slot], (round - 1) & 1, ST_TIMEOUT_EMPTY, W_PROD, true)) return false;
     if (stall_ns) *stall_ns += globaltimer_ns() - t0;
   }
   if (n >= static_cast<uint32_t>(INFLIGHT)) {
@@ -443,15 +447,7 @@ __device__ __noinline__ bool issue_piece(Smem &sm, WaitCtx w, uint32_t n, const 
     return false;
   }
   mbar_arrive_expect_tx(&sm.full[slot], bytes);
-  if (stage_row < 0) {
-    bulk_g2s(sm.ring[slot], src, bytes, &sm.full[slot], pol);
-  } else {
-    // Padded weight rows (see PIECE_BYTES): one copy per row.
-    const uint32_t rb = bytes / nrows;
-    uint8_t *dst = sm.ring[slot] + row_pad(stage_row);
-    for (int r = 0; r < nrows; ++r)
-      bulk_g2s(dst + r * (rb + 16), src + static_cast<size_t>(r) * rb, rb, &sm.full[slot], pol);
-  }
+  bulk_g2s(sm.ring[slot], src, bytes, &sm.full[slot], pol);
   return true;
 }
 
@@ -464,11 +460,8 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
 
   unsigned long long stall_ns = 0;
   const bool tracing = a.trace != nullptr;
-  int stage_row = -1;  // >= 0: the GEMV stage row index of the next padded piece
   auto issue = [&](const Piece &P) -> bool {
-    const bool ok = issue_piece(sm, w, n, P.src, P.bytes, P.nrows, stage_row, pol,
-                                tracing ? &stall_ns : nullptr);
-    if (stage_row >= 0) stage_row += P.nrows;
+    const bool ok = issue_piece(sm, w, n, P.src, P.bytes, pol, tracing ? &stall_ns : nullptr);
     ++n;
     return ok;
   };
@@ -490,9 +483,8 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
         tr[TR_P_START] = globaltimer_ns();
         tr[TR_P_STALL] = stall_ns;
       }
-      stage_row = 0;
       for (int i = 0; i < qg.total && ok; ++i) ok = issue(qkv_piece(qg, lp, i));
-      stage_row = -1;
+      if (tr) tr[TR_P_A_LAST] = globaltimer_ns();
       if (ok && ag.has && ag.npairs > 0) {
         // Cached tokens written earlier in this launch must be visible to the
         // bulk-copy engine: wait for every KV write of the previous steps.
@@ -509,14 +501,10 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
         }
         for (int i = 0; i < 2 * ag.npairs && ok; ++i) ok = issue(kv_piece(a, ag, l, i));
       }
-      stage_row = 0;
       for (int i = 0; i < o_np && ok; ++i) ok = issue(seg_piece(lp.w[6], 2 * QS, o_lo, o_n, i, 0));
-      stage_row = 0;
       for (int i = 0; i < 2 * gu_np && ok; ++i)
         ok = issue(seg_piece((i & 1) ? lp.w[9] : lp.w[8], 2 * H, gu_lo, gu_n, i >> 1, i & 1));
-      stage_row = 0;
       for (int i = 0; i < d_np && ok; ++i) ok = issue(seg_piece(lp.w[10], 2 * IM, o_lo, o_n, i, 0));
-      stage_row = -1;
       if (tr) tr[TR_P_END] = globaltimer_ns();
     }
     for (int i = 0; i < lm_np && ok; ++i) ok = issue(seg_piece(a.lm_head, 2 * H, lm_lo, lm_n, i, 0));
@@ -544,7 +532,7 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
 // barrier is needed between one stage's epilogue and the next table.
 template <int K, class GetPiece>
 __device__ __forceinline__ int prep_rows(Smem &sm, uint32_t n, int count, GetPiece get_piece) {
-  constexpr int PITCH = 2 * K + 16;
+  constexpr int PITCH = 2 * K;
   const int j = threadIdx.x;
   int total = 0;
   uint32_t addr0 = 0, my_addr = 0;
@@ -552,7 +540,7 @@ __device__ __forceinline__ int prep_rows(Smem &sm, uint32_t n, int count, GetPie
   bool found = false;
   for (int i = 0; i < count; ++i) {
     const Piece P = get_piece(i);
-    const uint32_t base = smem_u32(sm.ring[(n + i) % NSLOTS]) + row_pad(total);
+    const uint32_t base = smem_u32(sm.ring[(n + i) % NSLOTS]);
     if (i == 0) addr0 = base;
     if (!found && j < total + P.nrows) {
       my_addr = base + (j - total) * PITCH;
@@ -568,13 +556,6 @@ __device__ __forceinline__ int prep_rows(Smem &sm, uint32_t n, int count, GetPie
   return total;
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2,
-                                        uint32_t &a3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
-               : "r"(addr));
-}
-
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -584,66 +565,158 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Batch-1 GEMV of a stage on the tensor cores: y[j] = W[j,:] . x for the
-// `total` rows of the row table (pieces n .. n+count-1, all landed before
-// use).  The vector x (fp16[K], shared memory) is column 0 of the B operand;
-// rows are the A operand (ldmatrix from the padded ring rows); warp w takes
-// K/16/NCW of the K steps for all row tiles, and the per-warp partial sums
-// are added in a fixed order, so results are deterministic.  The tensor
-// cores here cut instruction count (the stage is latency- and HBM-bound);
-// fp16 products are exact and accumulate in fp32.
+__device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// Batch-1 GEMV of a stage with up to RMAX rows (QKV: <= 32, gate/up: <= 48
+// per CTA) on the CUDA cores: y[j] = W[j,:] . x for the `total` rows of the
+// row table (pieces n .. n+count-1, all landed before use).  Warp w takes
+// stage rows w, w + 8, ...; its lanes split K into 16-byte chunks (x's chunks
+// converted once and kept in registers), so each weight byte is read from
+// shared memory once, by consecutive lanes (no bank conflict, no row
+// padding).  fp16 products are exact in fp32; each lane keeps two fp32
+// chains, then a fixed-order warp sum: results are deterministic.
 // epi(kind, matrix_row, dot) runs on thread j for stage row j < total.
-template <int K, class Epi>
-__device__ __forceinline__ void gemv_mma(Smem &sm, uint32_t &n, int count, int total,
-                                         const __half *x, Epi epi, unsigned long long *tr = nullptr) {
-  constexpr int KS_W = K / 16 / NCW;
-  static_assert(KS_W % 2 == 0, "two accumulator chains");
+template <int K, int RMAX, class Epi>
+__device__ __forceinline__ void gemv_wr(Smem &sm, uint32_t &n, int count, int total,
+                                        const __half *x, Epi epi) {
+  constexpr int CH = K / 8 / 32;       // 16-byte chunks per lane
+  constexpr int RPW = RMAX / NCW;      // rows per warp
+  static_assert(K % 256 == 0 && RMAX % NCW == 0 && RMAX <= MAX_TILES * 16, "gemv_wr shape");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tiles = (total + 15) >> 4;
-  // Two independent accumulator chains per tile (even / odd K steps).
-  float d[MAX_TILES][4], e[MAX_TILES][4];
+  float xf[CH][8];
 #pragma unroll
-  for (int t = 0; t < MAX_TILES; ++t)
-    d[t][0] = d[t][1] = d[t][2] = d[t][3] = e[t][0] = e[t][1] = e[t][2] = e[t][3] = 0.f;
-  const int lrow = (lane & 7) + ((lane >> 3) & 1) * 8;
-  const uint32_t lcol = (lane >> 4) * 16;  // bytes
-  uint32_t rbase[MAX_TILES];
+  for (int i = 0; i < CH; ++i) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(x + 8 * (lane + 32 * i));
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
 #pragma unroll
-  for (int t = 0; t < MAX_TILES; ++t) rbase[t] = sm.rowaddr[t * 16 + lrow] + lcol;
-#pragma unroll 2
-  for (int q = 0; q < KS_W; q += 2) {
-    const int k0 = (warp * KS_W + q) * 16;
-    uint32_t b0 = 0, b1 = 0, c0 = 0, c1 = 0;
-    if (lane < 4) {
-      b0 = *reinterpret_cast<const uint32_t *>(x + k0 + 2 * lane);
-      b1 = *reinterpret_cast<const uint32_t *>(x + k0 + 8 + 2 * lane);
-      c0 = *reinterpret_cast<const uint32_t *>(x + k0 + 16 + 2 * lane);
-      c1 = *reinterpret_cast<const uint32_t *>(x + k0 + 24 + 2 * lane);
-    }
-#pragma unroll
-    for (int t = 0; t < MAX_TILES; ++t) {
-      if (t < tiles) {
-        uint32_t a0, a1, a2, a3, f0, f1, f2, f3;
-        ldsm_x4(rbase[t] + k0 * 2, a0, a1, a2, a3);
-        ldsm_x4(rbase[t] + k0 * 2 + 32, f0, f1, f2, f3);
-        mma16816(d[t], a0, a1, a2, a3, b0, b1);
-        mma16816(e[t], f0, f1, f2, f3, c0, c1);
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      xf[i][2 * j] = f.x;
+      xf[i][2 * j + 1] = f.y;
     }
   }
-  trace_clock(tr, TR_E_CYC1);
-  if ((lane & 3) == 0) {
+  float res[RPW];
 #pragma unroll
-    for (int t = 0; t < MAX_TILES; ++t) {
-      if (t < tiles) {
-        sm.mred[warp][t * 16 + (lane >> 2)] = d[t][0] + e[t][0];
-        sm.mred[warp][t * 16 + (lane >> 2) + 8] = d[t][2] + e[t][2];
+  for (int q = 0; q < RPW; ++q) {
+    // Rows >= total are padding entries pointing at row 0 (results unused).
+    const uint32_t row = sm.rowaddr[warp + NCW * q];
+    uint4 wv[CH];
+#pragma unroll
+    for (int i = 0; i < CH; ++i) wv[i] = lds_u4(row + 16u * (lane + 32 * i));
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const __half2 *h = reinterpret_cast<const __half2 *>(&wv[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        s0 = fmaf(f.x, xf[i][2 * j], s0);
+        s1 = fmaf(f.y, xf[i][2 * j + 1], s1);
       }
     }
+    res[q] = s0 + s1;
+  }
+#pragma unroll
+  for (int q = 0; q < RPW; ++q) res[q] = warp_sum(res[q]);
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < RPW; ++q) sm.mred[0][warp + NCW * q] = res[q];
   }
   named_bar_sync(BAR_ID, NCT);
-  if (lane == 0)
-    for (int i = 0; i < count; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
+  // Release the pieces: every warp arrives once per piece (lane i on piece i).
+  if (lane < count) mbar_arrive(&sm.empty[(n + lane) % NSLOTS]);
+  n += count;
+  if (tid < total) {
+    const int info = sm.rowinfo[tid];
+    epi(info >> 24, info & 0xffffff, sm.mred[0][tid]);
+  }
+}
+
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// GEMV of a stage with at most 8 rows (o_proj, down: 1024 rows over >= 128
+// CTAs) on the CUDA cores.  A tensor-core tile would waste 15 of its 16 rows
+// and read the padding from shared memory; here every weight byte is read
+// once: thread t takes the 4-element chunks t, t + 256, ... of every row (x's
+// chunks stay in registers), products are exact in fp32 and summed in fp32.
+// The per-row partials are reduce-scattered across the warp (lanes 4r..4r+3
+// end with row r), then added over the warps in a fixed order, so results
+// are deterministic.  epi(kind, matrix_row, dot) runs on thread j < total.
+template <int K, class Epi>
+__device__ __forceinline__ void gemv_cc(Smem &sm, uint32_t &n, int count, int total, const __half *x,
+                                        Epi epi, unsigned long long *tr = nullptr) {
+  constexpr int CH = K / 4 / NCT;  // chunks per thread
+  static_assert(K % (4 * NCT) == 0, "K must split into 4-element chunks over the consumer threads");
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float xf[CH][4];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(x + 4 * (tid + NCT * i));
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    xf[i][0] = lo.x;
+    xf[i][1] = lo.y;
+    xf[i][2] = hi.x;
+    xf[i][3] = hi.y;
+  }
+  // All loads first, with no branch between them (rows >= total are
+  // padding entries that point at row 0: valid memory, results unused).
+  uint2 wv[8][CH];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const uint32_t row = sm.rowaddr[r];
+#pragma unroll
+    for (int i = 0; i < CH; ++i) wv[r][i] = lds_u2(row + 8u * (tid + NCT * i));
+  }
+  float acc[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&wv[r][i].x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&wv[r][i].y));
+      s = fmaf(lo.x, xf[i][0], s);
+      s = fmaf(lo.y, xf[i][1], s);
+      s = fmaf(hi.x, xf[i][2], s);
+      s = fmaf(hi.y, xf[i][3], s);
+    }
+    acc[r] = s;
+  }
+  trace_clock(tr, TR_E_CYC1);
+  // Reduce-scatter over the warp: offsets 16, 8, 4 halve the rows a lane
+  // keeps; offsets 2, 1 finish the sum of the four lanes sharing a row.
+  float v4[4], v2[2];
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float keep = b16 ? acc[j + 4] : acc[j], send = b16 ? acc[j] : acc[j + 4];
+    v4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float keep = b8 ? v4[j + 2] : v4[j], send = b8 ? v4[j] : v4[j + 2];
+    v2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float v;
+  {
+    const float keep = b4 ? v2[1] : v2[0], send = b4 ? v2[0] : v2[1];
+    v = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  if ((lane & 3) == 0) sm.mred[warp][(b16 ? 4 : 0) + (b8 ? 2 : 0) + (b4 ? 1 : 0)] = v;
+  named_bar_sync(BAR_ID, NCT);
+  // Release the pieces: every warp arrives once per piece (lane i on piece i).
+  if (lane < count) mbar_arrive(&sm.empty[(n + lane) % NSLOTS]);
   n += count;
   if (tid < total) {
     float dot = 0.f;
@@ -729,6 +802,10 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
 #pragma unroll
   for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(nw + tid + NCT * i));
   st.fail |= !wait_pieces(sm, w, st.n, qg.total, W_A);
+  if (tr != nullptr) {
+    __syncwarp();
+    trace_mark(tr, TR_A_PIECES);
+  }
   if (l == 0) {
     const __half *emb = a.embed + static_cast<size_t>(token) * H;
 #pragma unroll
@@ -740,6 +817,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
     st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.hidden + tid + NCT * i; }, ep - 1, u, W_A);
 #pragma unroll
     for (int i = 0; i < 4; ++i) h[i] = __half2float(u2h(u[i]));
+    trace_mark(tr, TR_A_GATHER);
   }
   float ss = 0.f;
 #pragma unroll
@@ -752,7 +830,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
 #pragma unroll
   for (int i = 0; i < 4; ++i) sm.xa[tid + NCT * i] = __float2half(h[i] * (inv * wv[i]));
   named_bar_sync(BAR_ID, NCT);
-  gemv_mma<H>(
+  gemv_wr<H, 32>(
       sm, st.n, qg.total, total, sm.xa,
       [&](int kind, int row, float dot) {
         const __half hv = __float2half(dot);
@@ -834,23 +912,6 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
       if (warp < 2) sm.q_rot[warp][i] = hr;
       else sm.k_fresh[i] = hr;
     }
-    if (warp == 2 && ag.last) {
-      // New token's K (rotated) and V (raw) into the cache at position p,
-      // 8 bytes per lane; later steps of this launch read the entry with bulk
-      // copies, hence the proxy fence and the release count.
-      __syncwarp();
-      const size_t off = ((static_cast<size_t>(l) * NKV + g) * a.max_seq + p) * HD + 4 * lane;
-      *reinterpret_cast<uint2 *>(a.k_cache + off) = *reinterpret_cast<const uint2 *>(sm.k_fresh + 4 * lane);
-      *reinterpret_cast<uint2 *>(a.v_cache + off) =
-          *reinterpret_cast<const uint2 *>(sm.qkv_raw + 3 * HD + 4 * lane);
-      if (a.num_steps > 1) {
-        // Publication: __syncwarp orders the lanes' stores before lane 0's
-        // release; the reader acquires the count and issues a proxy fence
-        // before its bulk copy (see the producer).
-        __syncwarp();
-        if (lane == 0) red_release_add_u32(a.ws.kv_ready, 1);
-      }
-    }
   }
   named_bar_sync(BAR_ID, NCT);
 
@@ -867,10 +928,10 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     qa[kk][0] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][dim]) : 0u;
     qa[kk][1] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][dim + 2]) : 0u;
   }
-  const int hh = tid >> 7;                       // head of this thread (softmax, P.V)
-  const int dpair = tid & 63, par = (tid >> 6) & 1;  // P.V: dims 2*dpair..+1, token parity
-  float acc0 = 0.f, acc1 = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  const int hh = tid >> 7;                      // head of this thread in the softmax
+  const int dpair = tid & 63, ts = tid >> 6;    // P.V: dims 2*dpair..+1 of both heads, tokens = ts mod 4
+  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};   // [head][dim]
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // every thread tracks both heads
   const int total_old = ag.t1 - ag.t0;
   uint32_t n = st.n;
 #pragma unroll 1
@@ -916,11 +977,11 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
         const int t0 = tile * 8 + 2 * (lane & 3);
         const float s0 = d[0] * a.attn_scale, s1 = d[1] * a.attn_scale;
         if (t0 < ntok) {
-          sm.sc[lane >> 2][t0] = s0;
+          sm.sc[t0][lane >> 2] = s0;
           wmax = fmaxf(wmax, s0);
         }
         if (t0 + 1 < ntok) {
-          sm.sc[lane >> 2][t0 + 1] = s1;
+          sm.sc[t0 + 1][lane >> 2] = s1;
           wmax = fmaxf(wmax, s1);
         }
       }
@@ -929,97 +990,98 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, 2));
     if (lane == 0 || lane == 4) sm.wred[warp][lane >> 2] = wmax;
     named_bar_sync(BAR_ID, NCT);
-    if (sc == 0) trace_mark(tr, TR_B_SC);
-    // Softmax (expf as upstream, megakernel.cu:490-494): every thread of head
-    // hh derives the same running max, turns its tokens' scores into weights.
-    float cmax = -INFINITY;
+    if (sc == 0) {
+      trace_mark(tr, TR_B_SC);
+      trace_clock(tr, TR_B_CYC0);
+    }
+    // Softmax (expf as upstream, megakernel.cu:490-494): every thread derives
+    // the same running max of both heads; thread (hh, tt) turns its tokens'
+    // scores into weights.
+    float m_new[2];
 #pragma unroll
-    for (int i = 0; i < NCW; ++i) cmax = fmaxf(cmax, sm.wred[i][hh]);
-    const float m_new = fmaxf(m_run, cmax);
+    for (int h = 0; h < 2; ++h) {
+      float cmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NCW; ++i) cmax = fmaxf(cmax, sm.wred[i][h]);
+      m_new[h] = fmaxf(m_run[h], cmax);
+    }
     float psum = 0.f;
     if (ntok > 0) {
       for (int tt = tid & 127; tt < ntok; tt += 128) {
-        const float pr = expf(sm.sc[hh][tt] - m_new);
-        sm.sc[hh][tt] = pr;
+        const float pr = expf(sm.sc[tt][hh] - m_new[hh]);
+        sm.sc[tt][hh] = pr;
         psum += pr;
       }
     }
     psum = warp_sum(psum);
     if (lane == 0) sm.wsum[warp] = psum;
     named_bar_sync(BAR_ID, NCT);
-    {
+    if (sc == 0) trace_clock(tr, TR_B_CYC1);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
       float tsum = 0.f;
 #pragma unroll
-      for (int i = 0; i < NCW / 2; ++i) tsum += sm.wsum[hh * (NCW / 2) + i];
-      const float alpha = ntok == 0 ? 1.f : (m_run == -INFINITY ? 0.f : expf(m_run - m_new));
+      for (int i = 0; i < NCW / 2; ++i) tsum += sm.wsum[h * (NCW / 2) + i];
+      const float alpha = ntok == 0 ? 1.f : (m_run[h] == -INFINITY ? 0.f : expf(m_run[h] - m_new[h]));
       if (ntok > 0) {
-        l_run = l_run * alpha + tsum;
-        m_run = m_new;
+        l_run[h] = l_run[h] * alpha + tsum;
+        m_run[h] = m_new[h];
       }
-      acc0 *= alpha;
-      acc1 *= alpha;
+      acc[h][0] *= alpha;
+      acc[h][1] *= alpha;
     }
-    // P.V: dims 2*dpair, 2*dpair+1 of head hh over the tokens of parity par.
+    // P.V: thread (dpair, ts) adds dims 2*dpair, 2*dpair+1 of both heads over
+    // the tokens t = ts mod 4 (a V row is read once for both heads; pieces
+    // hold 48 tokens, a multiple of 4, so the residue is the same per piece).
     {
-      float b0 = 0.f, b1 = 0.f;
-      const float *pr = sm.sc[hh];
 #pragma unroll 1
       for (int t0 = 0; t0 < n_old; t0 += KV_TOK_PER_PIECE) {
         const uint32_t pn = n + 2 * (t0 / KV_TOK_PER_PIECE) + 1;
         const __half2 *vcol = reinterpret_cast<const __half2 *>(sm.ring[pn % NSLOTS]) + dpair;
+        const float2 *pr = reinterpret_cast<const float2 *>(sm.sc[t0]);
         const int cnt = min(KV_TOK_PER_PIECE, n_old - t0);
-        int tt = par;
-#pragma unroll 2
-        for (; tt + 2 < cnt; tt += 4) {
-          const float2 v0 = __half22float2(vcol[tt * (HD / 2)]);
-          const float2 v1 = __half22float2(vcol[(tt + 2) * (HD / 2)]);
-          const float p0 = pr[t0 + tt], p1 = pr[t0 + tt + 2];
-          acc0 = fmaf(p0, v0.x, acc0);
-          acc1 = fmaf(p0, v0.y, acc1);
-          b0 = fmaf(p1, v1.x, b0);
-          b1 = fmaf(p1, v1.y, b1);
-        }
-        for (; tt < cnt; tt += 2) {
-          const float2 v0 = __half22float2(vcol[tt * (HD / 2)]);
-          acc0 = fmaf(pr[t0 + tt], v0.x, acc0);
-          acc1 = fmaf(pr[t0 + tt], v0.y, acc1);
+#pragma unroll 4
+        for (int tt = ts; tt < cnt; tt += 4) {
+          const float2 v = __half22float2(vcol[tt * (HD / 2)]);
+          const float2 p = pr[tt];
+          acc[0][0] = fmaf(p.x, v.x, acc[0][0]);
+          acc[0][1] = fmaf(p.x, v.y, acc[0][1]);
+          acc[1][0] = fmaf(p.y, v.x, acc[1][0]);
+          acc[1][1] = fmaf(p.y, v.y, acc[1][1]);
         }
       }
-      if (fresh && par == (n_old & 1)) {
-        const float2 v0 = __half22float2(reinterpret_cast<const __half2 *>(sm.qkv_raw + 3 * HD)[dpair]);
-        acc0 = fmaf(pr[n_old], v0.x, acc0);
-        acc1 = fmaf(pr[n_old], v0.y, acc1);
+      if (fresh && ts == (n_old & 3)) {
+        const float2 v = __half22float2(reinterpret_cast<const __half2 *>(sm.qkv_raw + 3 * HD)[dpair]);
+        const float2 p = *reinterpret_cast<const float2 *>(sm.sc[n_old]);
+        acc[0][0] = fmaf(p.x, v.x, acc[0][0]);
+        acc[0][1] = fmaf(p.x, v.y, acc[0][1]);
+        acc[1][0] = fmaf(p.y, v.x, acc[1][0]);
+        acc[1][1] = fmaf(p.y, v.y, acc[1][1]);
       }
-      acc0 += b0;
-      acc1 += b1;
     }
+    if (sc == 0) trace_clock(tr, TR_B_CYC2);
     named_bar_sync(BAR_ID, NCT);
-    if (lane == 0)
-      for (int i = 0; i < 2 * npair; ++i) mbar_arrive(&sm.empty[(n + i) % NSLOTS]);
+    if (lane < 2 * npair) mbar_arrive(&sm.empty[(n + lane) % NSLOTS]);
     n += 2 * npair;
   }
   st.n = n;
   trace_mark(tr, TR_B_PV);
-  // Add the two token parities; thread (h, d) then holds output dim d of head h.
-  if (par == 1) {
-    sm.pv[hh][2 * dpair] = acc0;
-    sm.pv[hh][2 * dpair + 1] = acc1;
-  }
-  named_bar_sync(BAR_ID, NCT);
-  if (par == 0) {
-    sm.pv[hh][2 * dpair] += acc0;
-    sm.pv[hh][2 * dpair + 1] += acc1;
-    if (dpair == 0) {
-      sm.att_m[hh] = m_run;
-      sm.att_l[hh] = l_run;
-    }
+  trace_clock(tr, TR_B_CYC3);
+  // Add the four token slices in order; thread (h, d) then holds output dim
+  // d of head h.
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    *reinterpret_cast<float2 *>(&sm.pvp[ts][h][2 * dpair]) = make_float2(acc[h][0], acc[h][1]);
+  if (tid < 2) {
+    sm.att_m[tid] = m_run[tid];
+    sm.att_l[tid] = l_run[tid];
   }
   named_bar_sync(BAR_ID, NCT);
   const int dd = tid & 127;
-  const float acc = sm.pv[hh][dd];
+  const float acc_hd = ((sm.pvp[0][hh][dd] + sm.pvp[1][hh][dd]) + sm.pvp[2][hh][dd]) + sm.pvp[3][hh][dd];
   {
     const int h = hh, d = dd;
-    float val = acc;
+    float val = acc_hd;
     float m = sm.att_m[h], lsum = sm.att_l[h];
     if (ag.S > 1 && ag.j != 0) {
       uint64_t *pp = a.ws.part + ((static_cast<size_t>(g) * MAX_SPLITS + ag.j) * 2 + h) * (HD + 2);
@@ -1089,6 +1151,20 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
       a.attn_out[col] = o;
     }
   }
+  // New token's K (rotated) and V (raw) into the cache at position p, 8
+  // bytes per lane.  Later steps of this launch read the entry with bulk
+  // copies, hence the release count (the reader acquires it and issues a
+  // proxy fence before its copy).  Done last: the release waits for the
+  // stores, and nothing in this step reads the entry from global memory.
+  if (warp == 2 && ag.last) {
+    const size_t off = ((static_cast<size_t>(l) * NKV + g) * a.max_seq + p) * HD + 4 * lane;
+    *reinterpret_cast<uint2 *>(a.k_cache + off) = *reinterpret_cast<const uint2 *>(sm.k_fresh + 4 * lane);
+    *reinterpret_cast<uint2 *>(a.v_cache + off) = *reinterpret_cast<const uint2 *>(sm.qkv_raw + 3 * HD + 4 * lane);
+    if (a.num_steps > 1) {
+      __syncwarp();
+      if (lane == 0) red_release_add_u32(a.ws.kv_ready, 1);
+    }
+  }
   trace_mark(tr, TR_B2);
   return false;
 }
@@ -1112,7 +1188,7 @@ __device__ __forceinline__ bool stage_c(Smem &sm, const DecodeArgs &a, const Wai
   }
   if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
   trace_mark(tr, TR_C1);
-  gemv_mma<QS>(
+  gemv_cc<QS>(
       sm, st.n, np, total, sm.xb,
       [&](int, int row, float dot) {
         const float resid = __half2float(sm.hid_own[row - o.lo]);
@@ -1160,7 +1236,7 @@ __device__ __forceinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const Wai
   for (int i = 0; i < 4; ++i)
     sm.xa[tid + NCT * i] = __float2half(__half2float(__float2half(h[i])) * rstd * wv[i]);
   named_bar_sync(BAR_ID, NCT);
-  gemv_mma<H>(sm, st.n, np, total, sm.xa, [&](int kind, int row, float dot) {
+  gemv_wr<H, 48>(sm, st.n, np, total, sm.xa, [&](int kind, int row, float dot) {
     (kind == 0 ? sm.g_out : sm.u_out)[row - gu.lo] = dot;
   });
   named_bar_sync(BAR_ID, NCT);
@@ -1194,7 +1270,7 @@ __device__ __forceinline__ bool stage_e(Smem &sm, const DecodeArgs &a, const Wai
   if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
   trace_mark(tr, TR_E1);
   trace_clock(tr, TR_E_CYC0);
-  gemv_mma<IM>(
+  gemv_cc<IM>(
       sm, st.n, np, total, sm.xb,
       [&](int, int row, float dot) {
         const __half hv = __float2half(dot + sm.act_own[row - o.lo]);
@@ -1412,8 +1488,8 @@ out:
 
 __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 128-byte aligned base: the padded row layout relies on slot bases that
-  // are multiples of 128 bytes.
+  // 128-byte aligned base: bulk copies need 16-byte aligned slots, and the
+  // 16-byte vector reads of the GEMVs and of the K rows rely on it.
   // Offset the shared array itself rather than an integer copy of its
   // address: the compiler then keeps every Smem access in the shared address
   // space (LDS/STS instead of generic loads and stores).
