@@ -177,7 +177,7 @@ struct __align__(128) Smem {
   __half q_rot[2][HD];     // rotated q of the two heads (fp16, as upstream rounds it)
   float wred[NCW][2];      // per-warp score max per head
   float wsum[NCW];         // per-warp softmax sum
-  __align__(16) float pvp[4][2][HD];  // P.V partials of the four token slices [slice][head][dim]
+  __align__(16) float pvp[NCW][2][HD];  // P.V partials of the eight token slices [slice][head][dim]
   __align__(16) __half k_fresh[HD];
   __align__(16) float sc[SC_TOK + 1][2];  // scores, then softmax weights [token][head]
   float att_m[2], att_l[2], att_alpha[2];
@@ -929,8 +929,8 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     qa[kk][1] = lane < 8 ? *reinterpret_cast<const uint32_t *>(&sm.q_rot[lane >> 2][dim + 2]) : 0u;
   }
   const int hh = tid >> 7;                      // head of this thread in the softmax
-  const int dpair = tid & 63, ts = tid >> 6;    // P.V: dims 2*dpair..+1 of both heads, tokens = ts mod 4
-  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};   // [head][dim]
+  const int dq = lane, ts = warp;               // P.V: dims 4*dq..+3 of both heads, tokens = ts mod 8
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [head][dim]
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // every thread tracks both heads
   const int total_old = ag.t1 - ag.t0;
   uint32_t n = st.n;
@@ -966,13 +966,16 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
 #pragma unroll
       for (int b = 0; b < 4; ++b)
         kw[b] = *reinterpret_cast<const uint4 *>(krow + 32 * (b ^ (odd ? 1 : 0)) + 8 * (lane & 3));
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      // Two accumulator chains (the legacy MMA's latency dominates here).
+      float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
         const uint4 w = odd ? kw[b ^ 1] : kw[b];
         mma16816(d, qa[2 * b][0], 0u, qa[2 * b][1], 0u, w.x, w.y);
-        mma16816(d, qa[2 * b + 1][0], 0u, qa[2 * b + 1][1], 0u, w.z, w.w);
+        mma16816(e, qa[2 * b + 1][0], 0u, qa[2 * b + 1][1], 0u, w.z, w.w);
       }
+      d[0] += e[0];
+      d[1] += e[1];
       if (lane < 8) {
         const int t0 = tile * 8 + 2 * (lane & 3);
         const float s0 = d[0] * a.attn_scale, s1 = d[1] * a.attn_scale;
@@ -1027,37 +1030,37 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
         l_run[h] = l_run[h] * alpha + tsum;
         m_run[h] = m_new[h];
       }
-      acc[h][0] *= alpha;
-      acc[h][1] *= alpha;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[h][i] *= alpha;
     }
-    // P.V: thread (dpair, ts) adds dims 2*dpair, 2*dpair+1 of both heads over
-    // the tokens t = ts mod 4 (a V row is read once for both heads; pieces
-    // hold 48 tokens, a multiple of 4, so the residue is the same per piece).
+    // P.V: thread (dq, ts) adds dims 4*dq..4*dq+3 of both heads over the
+    // tokens t = ts mod 8 (a V row is read once for both heads; pieces hold
+    // 48 tokens, a multiple of 8, so the residue is the same per piece).
     {
+      auto pv_add = [&](const uint2 u, const float2 p) {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+        acc[0][0] = fmaf(p.x, lo.x, acc[0][0]);
+        acc[0][1] = fmaf(p.x, lo.y, acc[0][1]);
+        acc[0][2] = fmaf(p.x, hi.x, acc[0][2]);
+        acc[0][3] = fmaf(p.x, hi.y, acc[0][3]);
+        acc[1][0] = fmaf(p.y, lo.x, acc[1][0]);
+        acc[1][1] = fmaf(p.y, lo.y, acc[1][1]);
+        acc[1][2] = fmaf(p.y, hi.x, acc[1][2]);
+        acc[1][3] = fmaf(p.y, hi.y, acc[1][3]);
+      };
 #pragma unroll 1
       for (int t0 = 0; t0 < n_old; t0 += KV_TOK_PER_PIECE) {
         const uint32_t pn = n + 2 * (t0 / KV_TOK_PER_PIECE) + 1;
-        const __half2 *vcol = reinterpret_cast<const __half2 *>(sm.ring[pn % NSLOTS]) + dpair;
+        const uint2 *vcol = reinterpret_cast<const uint2 *>(sm.ring[pn % NSLOTS]) + dq;
         const float2 *pr = reinterpret_cast<const float2 *>(sm.sc[t0]);
         const int cnt = min(KV_TOK_PER_PIECE, n_old - t0);
-#pragma unroll 4
-        for (int tt = ts; tt < cnt; tt += 4) {
-          const float2 v = __half22float2(vcol[tt * (HD / 2)]);
-          const float2 p = pr[tt];
-          acc[0][0] = fmaf(p.x, v.x, acc[0][0]);
-          acc[0][1] = fmaf(p.x, v.y, acc[0][1]);
-          acc[1][0] = fmaf(p.y, v.x, acc[1][0]);
-          acc[1][1] = fmaf(p.y, v.y, acc[1][1]);
-        }
+#pragma unroll 2
+        for (int tt = ts; tt < cnt; tt += 8) pv_add(vcol[tt * (HD / 4)], pr[tt]);
       }
-      if (fresh && ts == (n_old & 3)) {
-        const float2 v = __half22float2(reinterpret_cast<const __half2 *>(sm.qkv_raw + 3 * HD)[dpair]);
-        const float2 p = *reinterpret_cast<const float2 *>(sm.sc[n_old]);
-        acc[0][0] = fmaf(p.x, v.x, acc[0][0]);
-        acc[0][1] = fmaf(p.x, v.y, acc[0][1]);
-        acc[1][0] = fmaf(p.y, v.x, acc[1][0]);
-        acc[1][1] = fmaf(p.y, v.y, acc[1][1]);
-      }
+      if (fresh && ts == (n_old & 7))
+        pv_add(reinterpret_cast<const uint2 *>(sm.qkv_raw + 3 * HD)[dq],
+               *reinterpret_cast<const float2 *>(sm.sc[n_old]));
     }
     if (sc == 0) trace_clock(tr, TR_B_CYC2);
     named_bar_sync(BAR_ID, NCT);
@@ -1067,18 +1070,20 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
   st.n = n;
   trace_mark(tr, TR_B_PV);
   trace_clock(tr, TR_B_CYC3);
-  // Add the four token slices in order; thread (h, d) then holds output dim
+  // Add the eight token slices in order; thread (h, d) then holds output dim
   // d of head h.
 #pragma unroll
   for (int h = 0; h < 2; ++h)
-    *reinterpret_cast<float2 *>(&sm.pvp[ts][h][2 * dpair]) = make_float2(acc[h][0], acc[h][1]);
+    *reinterpret_cast<float4 *>(&sm.pvp[ts][h][4 * dq]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   if (tid < 2) {
     sm.att_m[tid] = m_run[tid];
     sm.att_l[tid] = l_run[tid];
   }
   named_bar_sync(BAR_ID, NCT);
   const int dd = tid & 127;
-  const float acc_hd = ((sm.pvp[0][hh][dd] + sm.pvp[1][hh][dd]) + sm.pvp[2][hh][dd]) + sm.pvp[3][hh][dd];
+  float acc_hd = sm.pvp[0][hh][dd];
+#pragma unroll
+  for (int i = 1; i < NCW; ++i) acc_hd += sm.pvp[i][hh][dd];
   {
     const int h = hh, d = dd;
     float val = acc_hd;
@@ -1123,8 +1128,9 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
       // Rescale factors, once per (head, split): exp(m_j - M), M the max.
       if (tid < 2 * ag.S) {
         float M = -INFINITY;
-#pragma unroll 1
-        for (int jj = 0; jj < ag.S; ++jj) M = fmaxf(M, sm.cmb_m[hm][jj]);
+#pragma unroll
+        for (int jj = 0; jj < MAX_SPLITS_B200; ++jj)
+          if (jj < ag.S) M = fmaxf(M, sm.cmb_m[hm][jj]);
         const float mj = sm.cmb_m[hm][jm];
         sm.cmb_f[hm][jm] = mj == -INFINITY ? 0.f : expf(mj - M);
       }
