@@ -119,6 +119,27 @@ int launch_ldg_generate_nosync_static_ws(
     void *block_max_vals, void *block_max_idxs, int *output_log, int num_layers,
     int start_position, int max_seq_len, float attn_scale, void *stream);
 
+/*
+ * qwen_b200_decode_step_dev has no counterpart in the reference (upstream
+ * decodes greedily only).  One decode step like launch_ldg_decode_direct,
+ * except that the input token is read from device memory (*input_token, int32)
+ * when the kernel starts, and, when logits_out is not NULL, the fp32 logits of
+ * the step (norm_out @ lm_head^T, [151936]) are written there.  The greedy
+ * token still goes to *output_token.  With the sampler of qwen_b200_sample.h
+ * writing the next step's *input_token, sampled generation runs without a host
+ * round trip per token.  An input token outside [0, 151936) is a device-side
+ * error (status code 6, output -1).  Returns 0 when the launch was issued,
+ * else the qwen_b200_last_error() code.
+ */
+int qwen_b200_decode_step_dev(
+    const int *input_token, int *output_token, float *logits_out, const void *embed_weight,
+    const LDGLayerWeight *layer_weights, const void *final_norm_weight,
+    const void *lm_head_weight, const void *cos_table, const void *sin_table, void *k_cache,
+    void *v_cache, void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+    void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate, void *g_normalized,
+    void *block_max_vals, void *block_max_idxs, int num_layers, int position, int max_seq_len,
+    float attn_scale, void *stream);
+
 /* Error reporting (no upstream counterpart: the upstream megakernel launchers
  * return void and check no CUDA errors, qwen_ops.cpp:34-165).
  * qwen_b200_last_error: 0 if the calling thread's last launcher call was

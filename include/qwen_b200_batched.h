@@ -95,6 +95,14 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
                            const int *tokens_in, int *tokens_out, float *norm_out,
                            int max_position, float attn_scale, void *stream);
 
+/* The step above, with the tied lm_head's fp32 logits written to
+ * logits[r * ld + v] (ld >= 151936 and a multiple of 4, 16-byte aligned)
+ * instead of the fused argmax; feeds the sampler of qwen_b200_sample.h.  No
+ * upstream counterpart (upstream decodes greedily only). */
+int qwen_b200_batched_step_logits(void *handle, int rows, const int *seq_ids, const int *positions,
+                                  const int *tokens_in, float *logits, long long ld, float *norm_out,
+                                  int max_position, float attn_scale, void *stream);
+
 /* Synchronises the device; returns 0 if no batched kernel has recorded an
  * error since the last call, else its code (1: a bounded wait gave up, 2: a
  * token id outside the vocabulary, 3: a sequence id or position outside the

@@ -21,6 +21,7 @@ Differences from upstream, all deliberate:
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 import sys
@@ -77,6 +78,26 @@ def _assert_extension_compatibility() -> None:
 
 _assert_extension_compatibility()
 _decode = _require_megakernel_op("decode")
+
+
+_native = None
+
+
+def _native_lib():
+    """The C-ABI library (for the entry points the pybind module does not wrap)."""
+    global _native
+    if _native is None:
+        path = os.path.join(_HERE, "libqwen_b200.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: build it with qwen0.6b_b200/build.py")
+        L = ctypes.CDLL(path)
+        vp, i = ctypes.c_void_p, ctypes.c_int
+        L.qwen_b200_decode_step_dev.restype = i
+        L.qwen_b200_decode_step_dev.argtypes = [vp] * 22 + [i, i, i, ctypes.c_float, vp]
+        L.qwen_b200_last_error.restype = i
+        L.qwen_b200_last_error.argtypes = [ctypes.c_char_p, i]
+        _native = L
+    return _native
 
 
 def load_weights(model_name: str = "Qwen/Qwen3-0.6B", verbose: bool = True):
@@ -250,10 +271,54 @@ class Decoder:
         self._position += num_steps
         return out
 
-    def generate(self, prompt: str, max_tokens: int = 100) -> str:
+    def sample_ids(self, ids: list[int], max_tokens: int = 100, temperature: float = 1.0,
+                   top_k: int = 0, top_p: float = 1.0, seed: int = 0, reset: bool = True) -> list[int]:
+        """Sampled generation (no upstream counterpart; upstream is greedy
+        only): prefill ids[:-1] with step(), then per token one decode step
+        that reads its input token from device memory and writes the logits,
+        and one sampling launch that writes the next input token
+        (``sampling.py``: temperature, top-k, top-p as the transformers
+        warpers filter, Gumbel-max draw keyed by (seed, position)).  No host
+        round trip until the end."""
+        from sampling import SamplingParams, sample
+        if reset:
+            self.reset()
+        for tid in ids[:-1]:
+            self.step(tid)
+        if self._position + max_tokens > MAX_SEQ_LEN:
+            raise ValueError(f"{max_tokens} tokens from position {self._position} exceed {MAX_SEQ_LEN}")
+        dev = self._embed_weight.device
+        log = torch.empty(max_tokens + 1, dtype=torch.int32, device=dev)
+        log[0] = int(ids[-1])
+        logits = torch.empty(VOCAB_SIZE, dtype=torch.float32, device=dev)
+        params = SamplingParams(temperature, top_k, top_p, seed)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        L = _native_lib()
+        for n in range(max_tokens):
+            rc = L.qwen_b200_decode_step_dev(
+                log[n:].data_ptr(), self._out_token.data_ptr(), logits.data_ptr(),
+                *[t.data_ptr() for t in self._args()], self._num_layers, self._position,
+                MAX_SEQ_LEN, self._attn_scale, ctypes.c_void_p(stream))
+            if rc:
+                buf = ctypes.create_string_buffer(512)
+                L.qwen_b200_last_error(buf, 512)
+                raise RuntimeError(f"qwen_b200_decode_step_dev: {buf.value.decode()}")
+            sample(logits, params, offset=self._position, out=log[n + 1:n + 2])
+            self._position += 1
+        out = log[1:].cpu().tolist()
+        if any(t < 0 for t in out) or int(self._out_token.item()) < 0:
+            self._raise_device_failure("Decoder.sample_ids")
+        return out
+
+    def generate(self, prompt: str, max_tokens: int = 100, temperature: float = 0.0,
+                 top_k: int = 0, top_p: float = 1.0, seed: int = 0) -> str:
+        """Greedy as upstream (temperature 0, the default), else sampled."""
         self.reset()
         ids = self.tokenizer.encode(prompt, add_special_tokens=True)
-        out = self.generate_ids(ids, max_tokens, reset=False)
+        if temperature > 0.0 and top_k != 1:
+            out = self.sample_ids(ids, max_tokens, temperature, top_k, top_p, seed, reset=False)
+        else:
+            out = self.generate_ids(ids, max_tokens, reset=False)
         eos = self.tokenizer.eos_token_id
         if eos in out:
             out = out[: out.index(eos)]

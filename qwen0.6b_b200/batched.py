@@ -27,6 +27,7 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 _lib = None
 
 H, IM, NQ, NKV, HD = 1024, 3072, 16, 8, 128
+VOCAB = 151936
 
 
 class _Layer(ctypes.Structure):
@@ -49,6 +50,8 @@ def lib() -> ctypes.CDLL:
                                                vp, vp, vp, vp, i, i, i, vp, ll]
         L.qwen_b200_batched_step.restype = i
         L.qwen_b200_batched_step.argtypes = [vp, i, vp, vp, vp, vp, vp, i, ctypes.c_float, vp]
+        L.qwen_b200_batched_step_logits.restype = i
+        L.qwen_b200_batched_step_logits.argtypes = [vp, i, vp, vp, vp, vp, ll, vp, i, ctypes.c_float, vp]
         L.qwen_b200_batched_status.restype = i
         L.qwen_b200_batched_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64)]
         L.qwen_b200_batched_destroy.restype = None
@@ -148,10 +151,12 @@ class BatchedDecoder:
 
     def step(self, seq_ids: torch.Tensor, positions: torch.Tensor, tokens: torch.Tensor,
              max_position: int, norm_out: torch.Tensor | None = None,
-             out: torch.Tensor | None = None) -> torch.Tensor:
-        """One greedy step of rows = len(seq_ids) sequences (device int32
-        tensors).  Returns the device int32 tensor of produced tokens.  No host
-        synchronisation."""
+             out: torch.Tensor | None = None, sampling=None) -> torch.Tensor:
+        """One step of rows = len(seq_ids) sequences (device int32 tensors):
+        greedy, or drawn with ``sampling`` (a ``sampling.SamplingParams``; each
+        row's random stream is keyed by its sequence id and position, so a
+        draw does not depend on the batch composition).  Returns the device
+        int32 tensor of produced tokens.  No host synchronisation."""
         rows = int(seq_ids.numel())
         for t in (seq_ids, positions, tokens):
             if t.dtype != torch.int32 or t.device != self.dev or not t.is_contiguous():
@@ -159,6 +164,15 @@ class BatchedDecoder:
                                  f"{self.dev}")
         out = self.tokens_out[:rows] if out is None else out
         stream = torch.cuda.current_stream(self.dev).cuda_stream
+        if sampling is not None:
+            from sampling import sample
+            if getattr(self, "_logits", None) is None:
+                self._logits = torch.empty(self.max_rows, VOCAB, dtype=torch.float32, device=self.dev)
+            _check(lib().qwen_b200_batched_step_logits(
+                self._h, rows, seq_ids.data_ptr(), positions.data_ptr(), tokens.data_ptr(),
+                self._logits.data_ptr(), VOCAB, norm_out.data_ptr() if norm_out is not None else None,
+                int(max_position), self.attn_scale, ctypes.c_void_p(stream)), "batched_step_logits")
+            return sample(self._logits[:rows], sampling, out=out, row_seq=seq_ids, row_pos=positions)
         _check(lib().qwen_b200_batched_step(
             self._h, rows, seq_ids.data_ptr(), positions.data_ptr(), tokens.data_ptr(),
             out.data_ptr(), norm_out.data_ptr() if norm_out is not None else None,
@@ -204,9 +218,10 @@ class BatchedDecoder:
             self.step(ids, pos, tok, max(r[1] for r in chunk),
                       out=torch.empty(len(chunk), dtype=torch.int32, device=self.dev))
 
-    def generate(self, prompts: list[list[int]], max_tokens: int) -> list[list[int]]:
-        """Prefill, then `max_tokens` greedy steps of all sequences (at most
-        max_rows of them); returns the generated ids per sequence."""
+    def generate(self, prompts: list[list[int]], max_tokens: int, sampling=None) -> list[list[int]]:
+        """Prefill, then `max_tokens` steps of all sequences (at most max_rows
+        of them), greedy or with ``sampling``; returns the generated ids per
+        sequence."""
         if len(prompts) > self.max_rows:
             raise ValueError(f"{len(prompts)} sequences > max_rows={self.max_rows}")
         self.prefill(prompts)
@@ -220,7 +235,7 @@ class BatchedDecoder:
         outs = []
         for s in range(max_tokens):
             nxt = self.step(ids, pos, tok, start_max + s,
-                            out=torch.empty(n, dtype=torch.int32, device=self.dev))
+                            out=torch.empty(n, dtype=torch.int32, device=self.dev), sampling=sampling)
             outs.append(nxt)
             tok = nxt
             pos = pos + 1

@@ -627,18 +627,13 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
   return 0;
 }
 
-int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int *positions,
-                           const int *tokens_in, int *tokens_out, float *norm_out, int max_position,
-                           float attn_scale, void *stream) {
-  qb200_clear_error();
-  Plan *p = static_cast<Plan *>(handle);
-  if (p == nullptr) return fail(13, "null handle");
-  if (rows < 1 || rows > p->max_rows) return fail(10, "rows=%d out of range [1, %d]", rows, p->max_rows);
-  if (max_position < 0 || max_position >= p->max_seq)
-    return fail(11, "max_position=%d outside the KV cache (max_seq=%d)", max_position, p->max_seq);
-  if (seq_ids == nullptr || positions == nullptr || tokens_in == nullptr || tokens_out == nullptr)
-    return fail(13, "null pointer argument");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+namespace {
+
+// Every layer of a step plus the final RMSNorm (w.norm16 feeds the lm_head).
+int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, const int *tokens_in,
+                float *norm_out, int max_position, float attn_scale, cudaStream_t st) {
   const Workspace &w = p->ws;
   const int nb8 = (rows + 7) / 8;
   const int nsplit = max_position / CH + 1;
@@ -693,6 +688,34 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
   LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const __half *>(w.hidden),
          p->final_norm, w.norm16, norm_out, rows);
 #undef LAUNCH
+  return 0;
+}
+
+int check_step(Plan *p, int rows, const int *seq_ids, const int *positions, const int *tokens_in,
+               const void *out, int max_position) {
+  if (p == nullptr) return fail(13, "null handle");
+  if (rows < 1 || rows > p->max_rows) return fail(10, "rows=%d out of range [1, %d]", rows, p->max_rows);
+  if (max_position < 0 || max_position >= p->max_seq)
+    return fail(11, "max_position=%d outside the KV cache (max_seq=%d)", max_position, p->max_seq);
+  if (seq_ids == nullptr || positions == nullptr || tokens_in == nullptr || out == nullptr)
+    return fail(13, "null pointer argument");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int *positions,
+                           const int *tokens_in, int *tokens_out, float *norm_out, int max_position,
+                           float attn_scale, void *stream) {
+  qb200_clear_error();
+  Plan *p = static_cast<Plan *>(handle);
+  if (int rc = check_step(p, rows, seq_ids, positions, tokens_in, tokens_out, max_position)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace &w = p->ws;
+  if (int rc = step_layers(p, rows, seq_ids, positions, tokens_in, norm_out, max_position, attn_scale, st))
+    return rc;
   GemmArgs g{};
   g.M = rows;
   g.err = w.err;
@@ -704,6 +727,30 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
   if (int rc = qb200_gemm_run(p->g_lm, qb200tc::EPI_ARGMAX, g, st)) return rc;
   if (int rc = qb200_argmax_reduce(w.arg_val, w.arg_idx, p->lm_tiles, rows, tokens_out, st, true))
     return rc;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(20, "batched step launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+int qwen_b200_batched_step_logits(void *handle, int rows, const int *seq_ids, const int *positions,
+                                  const int *tokens_in, float *logits, long long ld, float *norm_out,
+                                  int max_position, float attn_scale, void *stream) {
+  qb200_clear_error();
+  Plan *p = static_cast<Plan *>(handle);
+  if (int rc = check_step(p, rows, seq_ids, positions, tokens_in, logits, max_position)) return rc;
+  if (ld < VOCAB || (ld & 3) != 0 || (reinterpret_cast<uintptr_t>(logits) & 15u) != 0)
+    return fail(14, "logits: ld=%lld must be >= %d and a multiple of 4, pointer 16-byte aligned", ld, VOCAB);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const Workspace &w = p->ws;
+  if (int rc = step_layers(p, rows, seq_ids, positions, tokens_in, norm_out, max_position, attn_scale, st))
+    return rc;
+  GemmArgs g{};
+  g.M = rows;
+  g.err = w.err;
+  g.pdl = 1;
+  g.out = logits;
+  g.ldo = static_cast<int>(ld);
+  if (int rc = qb200_gemm_run(p->g_lm, qb200tc::EPI_F32, g, st)) return rc;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(20, "batched step launch: %s", cudaGetErrorString(e));
   return 0;

@@ -88,6 +88,7 @@ enum Status : uint32_t {
   ST_TIMEOUT_EMPTY = 3,
   ST_TIMEOUT_KV = 4,
   ST_MISALIGNED = 5,
+  ST_BAD_TOKEN = 6,
 };
 enum Where : uint32_t { W_A = 1, W_B, W_C, W_D, W_E, W_F, W_G, W_PROD, W_SELFTEST };
 
@@ -125,6 +126,8 @@ struct DecodeArgs {
   int *bmax_idxs;
   int *out_tokens;
   int num_layers, start_pos, max_seq, num_steps, first_token;
+  const int *first_token_dev;  // when set: the first token is read from device memory
+  float *logits_out;           // when set: fp32 [VOCAB] logits of the last step
   float attn_scale;
   uint32_t epoch_base;
   long long timeout_ns;
@@ -1357,6 +1360,7 @@ __device__ __forceinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const Wai
         }
         const float v = warp_sum(acc0 + acc1);
         const int idx = P.row0 + r;
+        if (a.logits_out != nullptr && lane == 0 && s == a.num_steps - 1) a.logits_out[idx] = v;
         if (v > best || (v == best && idx < bidx)) {
           best = v;
           bidx = idx;
@@ -1460,6 +1464,13 @@ __device__ __forceinline__ void consumer(const DecodeArgs &a, Smem &sm) {
   st.n = 0;
   st.fail = false;
   int token = a.first_token;
+  if (a.first_token_dev != nullptr) {
+    token = *reinterpret_cast<const volatile int *>(a.first_token_dev);
+    if (token < 0 || token >= VOCAB) {
+      set_error(w, ST_BAD_TOKEN, W_A);
+      token = 0;
+    }
+  }
   int s = 0;
   for (s = 0; s < a.num_steps; ++s) {
     const int p = a.start_pos + s;
@@ -1711,7 +1722,7 @@ int check_args(const DecodeArgs &a) {
     return fail_msg(11,
                     "positions %d..%d exceed max_seq_len=%d (the KV cache has no slot for them)",
                     a.start_pos, a.start_pos + a.num_steps - 1, a.max_seq);
-  if (a.first_token < 0 || a.first_token >= VOCAB)
+  if (a.first_token_dev == nullptr && (a.first_token < 0 || a.first_token >= VOCAB))
     return fail_msg(12, "token id %d outside [0, %d)", a.first_token, VOCAB);
   const void *ptrs[] = {a.embed, a.layers, a.final_norm, a.lm_head, a.cos_t, a.sin_t, a.k_cache,
                         a.v_cache, a.hidden, a.act, a.res, a.q, a.k, a.v, a.attn_out, a.inter,
@@ -1926,6 +1937,29 @@ void launch_ldg_generate_nosync(int first_token_id, int num_steps, const void *e
                                block_max_idxs, output_log, num_layers, start_position,
                                max_seq_len, attn_scale);
   launch_decode(a, static_cast<cudaStream_t>(stream));
+}
+
+int qwen_b200_decode_step_dev(const int *input_token, int *output_token, float *logits_out,
+                              const void *embed_weight, const LDGLayerWeight *layer_weights,
+                              const void *final_norm_weight, const void *lm_head_weight,
+                              const void *cos_table, const void *sin_table, void *k_cache, void *v_cache,
+                              void *hidden_buffer, void *g_activations, void *g_residual, void *g_q,
+                              void *g_k, void *g_v, void *g_attn_out, void *g_mlp_intermediate,
+                              void *g_normalized, void *block_max_vals, void *block_max_idxs,
+                              int num_layers, int position, int max_seq_len, float attn_scale,
+                              void *stream) {
+  if (input_token == nullptr) {
+    qb200_clear_error();
+    return fail_msg(13, "null input token pointer");
+  }
+  DecodeArgs a = generate_args(0, 1, embed_weight, layer_weights, final_norm_weight, lm_head_weight,
+                               cos_table, sin_table, k_cache, v_cache, hidden_buffer, g_activations,
+                               g_residual, g_q, g_k, g_v, g_attn_out, g_mlp_intermediate, g_normalized,
+                               block_max_vals, block_max_idxs, output_token, num_layers, position,
+                               max_seq_len, attn_scale);
+  a.first_token_dev = input_token;
+  a.logits_out = logits_out;
+  return launch_decode(a, static_cast<cudaStream_t>(stream));
 }
 
 int launch_ldg_generate_nosync_static_ws(
