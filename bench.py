@@ -434,6 +434,97 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
         dist.destroy_process_group()
 
 
+def run_sample(args, world: int, rank: int, local: int, dev, dist) -> None:
+    """Sampling on logits rows (no upstream counterpart; upstream is greedy
+    only): temperature 0.8, top-k 50, top-p 0.9 over [B, 151936] fp32 logits,
+    the transformers warpers' semantics, one token per row.  One step = one
+    call on B rows; 4 logits buffers rotate."""
+    from sampling import SamplingParams, sample
+    B, V = args.batch, 151936
+    params = SamplingParams(0.8, 50, 0.9, seed=7)
+    g = torch.Generator(device=dev).manual_seed(SEED + rank)
+    bufs = [3.0 * torch.randn(B, V, generator=g, device=dev) for _ in range(4)]
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        sample(bufs[i % 4], params, offset=i, out=out)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        sample(bufs[i % 4], params, offset=i, out=out)
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    h_l = bufs[0].cpu().pin_memory()
+    h_t = torch.empty(B, dtype=torch.int32).pin_memory()
+    d_l = torch.empty_like(bufs[0])
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        d_l.copy_(h_l, non_blocking=True)
+        h_t.copy_(sample(d_l, params, offset=i, out=out), non_blocking=True)
+        stream.synchronize()
+    e2e_ms = 1000.0 * (time.perf_counter() - t0)
+    if dist is not None:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    value = world * B * args.steps / (total_ms / 1000.0)
+    alg = B * V * 4
+    avg_step_s = statistics.mean(step_ms) / 1000.0
+    peaks = measured_peaks()
+    achieved = alg / avg_step_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (logits ~ 3 N(0,1))",
+        "config": {"workload": f"sampling (temperature 0.8, top-k 50, top-p 0.9) of {B} rows x {V} logits",
+                   "batch": B, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "4 logits buffers rotate" + (" (> L2 each)" if B * V * 4 > 126e6 else
+                                                      " (L2-resident, as right after the lm_head)")},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
+                     "algorithmic_bytes_per_step": alg, "avg_step_ms": avg_step_s * 1000.0,
+                     "note": "algorithmic bytes = one read of the logits; the radix selection reads them "
+                             "about 5 times"},
+        "e2e": {"value": world * B * args.steps / (e2e_ms / 1000.0), "unit": "rows/s",
+                "h2d_bytes_per_step": B * V * 4, "d2h_bytes_per_step": B * 4},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from transformers.generation.logits_process import (TemperatureLogitsWarper, TopKLogitsWarper,
+                                                            TopPLogitsWarper)
+        threads = torch.get_num_threads()
+        x = bufs[0][: min(B, 16)].cpu()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0 or n < 1:
+            sc = TopPLogitsWarper(0.9)(None, TopKLogitsWarper(50)(None, TemperatureLogitsWarper(0.8)(None, x)))
+            torch.multinomial(torch.softmax(sc, -1), 1)
+            n += 1
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": x.shape[0] * n / dt, "unit": "rows/s", "cores": threads,
+                                "kind": "port",
+                                "sample": f"{n} calls of the transformers warpers + torch.multinomial on "
+                                          f"{x.shape[0]} rows on the host ({dt:.1f} s)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
     """Config 5: tied lm_head + greedy argmax with the vocabulary split over the
     ranks (one contiguous row block each), the (max, index) pairs all-gathered
@@ -546,11 +637,13 @@ def main() -> None:
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prefilled tokens before the timed steps (workload: 1920)")
     ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "ops", "batched", "lmhead"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "ops", "batched", "lmhead", "sample"],
                     help="decode: config 2 (default); ops: config 3; batched: config 4; lmhead: config 5")
     ap.add_argument("--batch", type=int, default=256, help="rows per step (ops, lmhead workloads)")
     ap.add_argument("--layers", type=int, default=28,
                     help="model depth of the batched workload; fewer layers only for profiling captures")
+    ap.add_argument("--sampled", action="store_true",
+                    help="decode workload: sample (temperature 0.8, top-k 50, top-p 0.9) instead of greedy")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
@@ -584,6 +677,9 @@ def main() -> None:
     if args.workload == "ops":
         run_ops(args, world, rank, local, dev, dist)
         return
+    if args.workload == "sample":
+        run_sample(args, world, rank, local, dev, dist)
+        return
 
     from Qwen06B_architecture import Decoder
     from qwen_weights import synthetic_weights
@@ -606,6 +702,8 @@ def main() -> None:
 
     def one_step():
         dec._position = plen
+        if args.sampled:
+            return dec.sample_nosync(first, gen, temperature=0.8, top_k=50, top_p=0.9, seed=7)
         return dec.generate_nosync(first, gen)
 
     for _ in range(args.warmup):
@@ -647,8 +745,7 @@ def main() -> None:
     for i in range(args.steps):
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        dec._position = plen
-        toks = dec.generate_nosync(first, gen).cpu()
+        toks = one_step().cpu()
         e2e_ms.append(1000.0 * (time.perf_counter() - t0))
         assert toks.tolist() == ref_tokens
 
@@ -671,7 +768,8 @@ def main() -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded random-init weights, uniform-random token ids)",
-        "config": {"workload": f"config 2: batch-1 greedy decode, {plen}-token seeded prompt "
+        "config": {"workload": f"config 2: batch-1 {'sampled (temperature 0.8, top-k 50, top-p 0.9)' if args.sampled else 'greedy'}"
+                               f" decode, {plen}-token seeded prompt "
                                f"prefilled (untimed), {gen} steps at positions {plen}..{plen + gen - 1}"
                                " per step",
                    "batch": 1, "prompt_len": plen, "gen_steps": gen,
@@ -683,9 +781,11 @@ def main() -> None:
                      "algorithmic_bytes_per_launch": alg, "avg_launch_ms": avg_launch_s * 1000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * gen},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 * gen if args.sampled else 1),
         "clocks": clk,
     }
+    if args.sampled:
+        line["roofline"]["note"] = "per token: one decode launch (logits written) + one sampling launch"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w_cpu)
     if rank == 0:

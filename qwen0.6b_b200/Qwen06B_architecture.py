@@ -271,41 +271,47 @@ class Decoder:
         self._position += num_steps
         return out
 
-    def sample_ids(self, ids: list[int], max_tokens: int = 100, temperature: float = 1.0,
-                   top_k: int = 0, top_p: float = 1.0, seed: int = 0, reset: bool = True) -> list[int]:
-        """Sampled generation (no upstream counterpart; upstream is greedy
-        only): prefill ids[:-1] with step(), then per token one decode step
-        that reads its input token from device memory and writes the logits,
-        and one sampling launch that writes the next input token
+    def sample_nosync(self, first_token: int, num_steps: int, temperature: float = 1.0,
+                      top_k: int = 0, top_p: float = 1.0, seed: int = 0) -> torch.Tensor:
+        """Sampled counterpart of ``generate_nosync`` (no upstream counterpart;
+        upstream is greedy only): from the current position, per token one
+        decode step that reads its input token from device memory and writes
+        the logits, and one sampling launch that writes the next input token
         (``sampling.py``: temperature, top-k, top-p as the transformers
-        warpers filter, Gumbel-max draw keyed by (seed, position)).  No host
-        round trip until the end."""
+        warpers filter, Gumbel-max draw keyed by (seed, position)).  Returns
+        the device int32 tokens; no host synchronisation."""
         from sampling import SamplingParams, sample
-        if reset:
-            self.reset()
-        for tid in ids[:-1]:
-            self.step(tid)
-        if self._position + max_tokens > MAX_SEQ_LEN:
-            raise ValueError(f"{max_tokens} tokens from position {self._position} exceed {MAX_SEQ_LEN}")
+        if self._position + num_steps > MAX_SEQ_LEN:
+            raise ValueError(f"{num_steps} tokens from position {self._position} exceed {MAX_SEQ_LEN}")
         dev = self._embed_weight.device
-        log = torch.empty(max_tokens + 1, dtype=torch.int32, device=dev)
-        log[0] = int(ids[-1])
-        logits = torch.empty(VOCAB_SIZE, dtype=torch.float32, device=dev)
+        log = torch.empty(num_steps + 1, dtype=torch.int32, device=dev)
+        log[0] = int(first_token)
+        if getattr(self, "_logits", None) is None:
+            self._logits = torch.empty(VOCAB_SIZE, dtype=torch.float32, device=dev)
         params = SamplingParams(temperature, top_k, top_p, seed)
         stream = torch.cuda.current_stream(dev).cuda_stream
         L = _native_lib()
-        for n in range(max_tokens):
+        ptrs = [t.data_ptr() for t in self._args()]
+        for n in range(num_steps):
             rc = L.qwen_b200_decode_step_dev(
-                log[n:].data_ptr(), self._out_token.data_ptr(), logits.data_ptr(),
-                *[t.data_ptr() for t in self._args()], self._num_layers, self._position,
-                MAX_SEQ_LEN, self._attn_scale, ctypes.c_void_p(stream))
+                log[n:].data_ptr(), self._out_token.data_ptr(), self._logits.data_ptr(), *ptrs,
+                self._num_layers, self._position, MAX_SEQ_LEN, self._attn_scale, ctypes.c_void_p(stream))
             if rc:
                 buf = ctypes.create_string_buffer(512)
                 L.qwen_b200_last_error(buf, 512)
                 raise RuntimeError(f"qwen_b200_decode_step_dev: {buf.value.decode()}")
-            sample(logits, params, offset=self._position, out=log[n + 1:n + 2])
+            sample(self._logits, params, offset=self._position, out=log[n + 1:n + 2])
             self._position += 1
-        out = log[1:].cpu().tolist()
+        return log[1:]
+
+    def sample_ids(self, ids: list[int], max_tokens: int = 100, temperature: float = 1.0,
+                   top_k: int = 0, top_p: float = 1.0, seed: int = 0, reset: bool = True) -> list[int]:
+        """Prefill ids[:-1] with step(), then ``sample_nosync`` from ids[-1]."""
+        if reset:
+            self.reset()
+        for tid in ids[:-1]:
+            self.step(tid)
+        out = self.sample_nosync(ids[-1], max_tokens, temperature, top_k, top_p, seed).cpu().tolist()
         if any(t < 0 for t in out) or int(self._out_token.item()) < 0:
             self._raise_device_failure("Decoder.sample_ids")
         return out
