@@ -80,6 +80,24 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
                              int max_seq, int max_rows, void *workspace,
                              long long workspace_bytes);
 
+/* Paged KV pools (no upstream counterpart; upstream has one contiguous
+ * 2048-token cache, Model/Qwen06B_architecture.py:21, :233-237): k_pool /
+ * v_pool are fp16 [num_pages][num_layers][8][128][128], pages of 128 tokens
+ * shared by all sequences; page_table is a device int32
+ * [num_seqs][max_pages_per_seq] array owned and updated by the caller (entry
+ * = the page holding positions [128 i, 128 i + 128) of that sequence, or -1).
+ * A step reads the table when it runs: pages must be mapped before a step
+ * touches their positions (an unmapped page is a recorded error, code 3, and
+ * the access is skipped).  max_seq may exceed 2048 (up to 65536) as long as
+ * max_pages_per_seq * 128 >= max_seq and the RoPE tables have max_seq rows.
+ * Everything else as qwen_b200_batched_create. */
+int qwen_b200_batched_create_paged(void **handle, const QwenBatchedLayer *layers, int num_layers,
+                                   const void *embed, const void *final_norm, const void *cos_table,
+                                   const void *sin_table, void *k_pool, void *v_pool, int num_pages,
+                                   const int *page_table, int max_pages_per_seq, int num_seqs,
+                                   int max_seq, int max_rows, void *workspace,
+                                   long long workspace_bytes);
+
 /* One greedy step for `rows` rows (device int32 arrays): row r is sequence
  * seq_ids[r] at position positions[r], fed token tokens_in[r]; K/V of that
  * position are appended to its cache, the argmax token is written to

@@ -48,6 +48,9 @@ def lib() -> ctypes.CDLL:
         L.qwen_b200_batched_create.restype = i
         L.qwen_b200_batched_create.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(_Layer), i, vp, vp,
                                                vp, vp, vp, vp, i, i, i, vp, ll]
+        L.qwen_b200_batched_create_paged.restype = i
+        L.qwen_b200_batched_create_paged.argtypes = [ctypes.POINTER(vp), ctypes.POINTER(_Layer), i, vp, vp,
+                                                     vp, vp, vp, vp, i, vp, i, i, i, i, vp, ll]
         L.qwen_b200_batched_step.restype = i
         L.qwen_b200_batched_step.argtypes = [vp, i, vp, vp, vp, vp, vp, i, ctypes.c_float, vp]
         L.qwen_b200_batched_step_logits.restype = i
@@ -87,17 +90,63 @@ def pack_layer(lw: list) -> dict:
                 w_gu=w_gu, w_down=down.contiguous())
 
 
+PAGE = 128  # tokens per KV page (the attention split length)
+
+
+class PagePool:
+    """Host bookkeeping of paged KV pools: which page holds positions
+    [128 i, 128 i + 128) of each sequence (-1: none), and the free pages."""
+
+    def __init__(self, num_pages: int, num_seqs: int, max_pages: int):
+        self.num_pages, self.num_seqs, self.max_pages = num_pages, num_seqs, max_pages
+        self.table = [[-1] * max_pages for _ in range(num_seqs)]
+        self.free = list(range(num_pages - 1, -1, -1))  # pop() hands out the lowest page first
+
+    def reserve(self, seq: int, upto_position: int) -> bool:
+        """Maps pages for positions 0..upto_position; True if the row changed."""
+        need = upto_position // PAGE + 1
+        if not 0 <= seq < self.num_seqs or not 0 <= upto_position or need > self.max_pages:
+            raise ValueError(f"sequence {seq} / position {upto_position} outside the page table")
+        row = self.table[seq]
+        missing = [i for i in range(need) if row[i] < 0]
+        if len(missing) > len(self.free):
+            raise RuntimeError(f"KV page pool exhausted ({self.num_pages} pages of {PAGE} tokens)")
+        for i in missing:
+            row[i] = self.free.pop()
+        return bool(missing)
+
+    def release(self, seq: int) -> None:
+        row = self.table[seq]
+        for i, pg in enumerate(row):
+            if pg >= 0:
+                self.free.append(pg)
+                row[i] = -1
+
+    @property
+    def in_use(self) -> int:
+        return self.num_pages - len(self.free)
+
+
 class BatchedDecoder:
-    """Greedy decode of `num_seqs` independent sequences on one GPU.
+    """Greedy (or sampled) decode of `num_seqs` independent sequences on one GPU.
 
     weights: the ``load_weights`` dict (``embed_weight``, ``layer_weights``,
     ``final_norm_weight``, ``cos_table``, ``sin_table``), any device.
-    Sequence s owns ``k_pool[s]`` / ``v_pool[s]`` (fp16 [layers, 8, max_seq, 128]).
+    Contiguous pools (default): sequence s owns ``k_pool[s]`` / ``v_pool[s]``
+    (fp16 [layers, 8, max_seq, 128], the upstream per-sequence layout).
+    Paged pools (``paged=True``, no upstream counterpart): ``num_pages`` pages
+    of 128 tokens (fp16 [num_pages, layers, 8, 128, 128] for K and for V)
+    shared by all sequences through ``page_table`` (int32 [num_seqs,
+    max_seq / 128], -1 = unmapped); ``reserve`` maps pages before positions
+    are used (``prefill``, ``prefill_parallel`` and ``generate`` do it), and
+    ``release`` returns a finished sequence's pages.  max_seq may then exceed
+    2048 (RoPE tables are rebuilt to max_seq rows when the weights' are shorter).
     """
 
     def __init__(self, weights: dict, num_seqs: int, max_rows: int | None = None,
                  max_seq: int = 2048, num_layers: int | None = None, device=None,
-                 k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None):
+                 k_pool: torch.Tensor | None = None, v_pool: torch.Tensor | None = None,
+                 paged: bool = False, num_pages: int | None = None):
         self.dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         lw = weights["layer_weights"]
         self.L = num_layers or len(lw) // 11
@@ -109,10 +158,23 @@ class BatchedDecoder:
         self.final_norm = weights["final_norm_weight"].to(**to).contiguous()
         self.cos = weights["cos_table"].to(**to).contiguous()
         self.sin = weights["sin_table"].to(**to).contiguous()
+        if self.cos.shape[0] < max_seq:
+            from qwen_weights import rope_tables
+            cos, sin = rope_tables(max_seq)
+            self.cos, self.sin = cos.to(**to), sin.to(**to)
         self.layers = [pack_layer([t.to(**to) for t in lw[11 * l: 11 * l + 11]]) for l in range(self.L)]
         # Positions a sequence has not reached are never read, so the pools need no clearing.
         # Caller-owned pools (e.g. a Decoder's own cache) must have this exact layout.
         shape = (num_seqs, self.L, NKV, max_seq, HD)
+        self.paged = bool(paged)
+        if self.paged:
+            if k_pool is not None or v_pool is not None:
+                raise ValueError("caller-owned pools are contiguous only")
+            self.max_pages = (max_seq + PAGE - 1) // PAGE
+            self.num_pages = int(num_pages) if num_pages else num_seqs * self.max_pages
+            shape = (self.num_pages, self.L, NKV, PAGE, HD)
+            self.page_table = torch.full((num_seqs, self.max_pages), -1, dtype=torch.int32, **to)
+            self.pages = PagePool(self.num_pages, num_seqs, self.max_pages)
         if k_pool is not None or v_pool is not None:
             for t in (k_pool, v_pool):
                 if (t is None or tuple(t.shape) != shape or t.dtype != torch.float16
@@ -132,11 +194,40 @@ class BatchedDecoder:
                 setattr(arr[l], name[0], d[name[0]].data_ptr())
         h = ctypes.c_void_p()
         with torch.cuda.device(self.dev):
-            _check(lib().qwen_b200_batched_create(
-                ctypes.byref(h), arr, self.L, self.embed.data_ptr(), self.final_norm.data_ptr(),
-                self.cos.data_ptr(), self.sin.data_ptr(), self.k_pool.data_ptr(), self.v_pool.data_ptr(),
-                num_seqs, max_seq, self.max_rows, self.workspace.data_ptr(), ws), "batched_create")
+            if self.paged:
+                _check(lib().qwen_b200_batched_create_paged(
+                    ctypes.byref(h), arr, self.L, self.embed.data_ptr(), self.final_norm.data_ptr(),
+                    self.cos.data_ptr(), self.sin.data_ptr(), self.k_pool.data_ptr(), self.v_pool.data_ptr(),
+                    self.num_pages, self.page_table.data_ptr(), self.max_pages, num_seqs, max_seq,
+                    self.max_rows, self.workspace.data_ptr(), ws), "batched_create_paged")
+            else:
+                _check(lib().qwen_b200_batched_create(
+                    ctypes.byref(h), arr, self.L, self.embed.data_ptr(), self.final_norm.data_ptr(),
+                    self.cos.data_ptr(), self.sin.data_ptr(), self.k_pool.data_ptr(), self.v_pool.data_ptr(),
+                    num_seqs, max_seq, self.max_rows, self.workspace.data_ptr(), ws), "batched_create")
         self._h = h
+
+    # ----------------------------------------------------------- paged pools
+    def reserve(self, seq: int, upto_position: int) -> None:
+        """Maps pages for positions 0..upto_position of sequence `seq` (paged
+        pools; a no-op otherwise).  Raises when the pool is exhausted."""
+        if not self.paged:
+            return
+        if not 0 <= upto_position < self.max_seq:
+            raise ValueError(f"position {upto_position} outside [0, {self.max_seq})")
+        if self.pages.reserve(seq, upto_position):
+            self.page_table[seq].copy_(torch.tensor(self.pages.table[seq], dtype=torch.int32))
+
+    def release(self, seq: int) -> None:
+        """Returns every page of sequence `seq` to the pool (paged pools)."""
+        if not self.paged:
+            return
+        self.pages.release(seq)
+        self.page_table[seq].fill_(-1)
+
+    @property
+    def pages_in_use(self) -> int:
+        return self.pages.in_use if self.paged else 0
 
     def close(self) -> None:
         if getattr(self, "_h", None):
@@ -193,6 +284,8 @@ class BatchedDecoder:
             live = [i for i, p in enumerate(prompts) if t < len(p) - 1]
             for c0 in range(0, len(live), self.max_rows):
                 chunk = live[c0: c0 + self.max_rows]
+                for i in chunk:
+                    self.reserve(seqs[i], t)
                 ids = torch.tensor([seqs[i] for i in chunk], dtype=torch.int32, device=self.dev)
                 pos = torch.full((len(chunk),), t, dtype=torch.int32, device=self.dev)
                 tok = torch.tensor([prompts[i][t] for i in chunk], dtype=torch.int32, device=self.dev)
@@ -212,6 +305,8 @@ class BatchedDecoder:
         rows = [(seqs[i], starts[i] + t, p[t]) for i, p in enumerate(prompts) for t in range(len(p) - 1)]
         for c0 in range(0, len(rows), self.max_rows):
             chunk = rows[c0: c0 + self.max_rows]
+            for r in chunk:
+                self.reserve(r[0], r[1])
             ids = torch.tensor([r[0] for r in chunk], dtype=torch.int32, device=self.dev)
             pos = torch.tensor([r[1] for r in chunk], dtype=torch.int32, device=self.dev)
             tok = torch.tensor([r[2] for r in chunk], dtype=torch.int32, device=self.dev)
@@ -233,6 +328,8 @@ class BatchedDecoder:
         if start_max + max_tokens > self.max_seq:
             raise ValueError("generation would run past max_seq")
         outs = []
+        for i, p in enumerate(prompts):
+            self.reserve(i, len(p) - 1 + max_tokens - 1)
         for s in range(max_tokens):
             nxt = self.step(ids, pos, tok, start_max + s,
                             out=torch.empty(n, dtype=torch.int32, device=self.dev), sampling=sampling)

@@ -66,6 +66,27 @@ __device__ __noinline__ void record_err(unsigned long long *err, uint32_t code) 
   atomicCAS(err, 0ull, v);
 }
 
+// KV pool geometry.  Contiguous pools: page = sequence, one page of max_seq
+// tokens per (sequence, layer, kv head).  Paged pools: pages of CH tokens,
+// page_table[seq * max_pages + position / CH] names the page of a position
+// (-1: none).  Pool row of (sequence, layer, kv head g, position):
+// ((page * layers + layer) * 8 + g) * page_tokens + position % page_tokens.
+struct KvGeom {
+  const int *page_table;  // null: contiguous pools
+  int max_pages, num_pages, page_tokens, num_layers;
+};
+
+// Pool row of token `pos` of kv head g, or -1 when its page is not mapped.
+__device__ __forceinline__ long long kv_row(const KvGeom &kg, int seq, int layer, int g, int pos) {
+  int page = seq, off = pos;
+  if (kg.page_table != nullptr) {
+    page = kg.page_table[static_cast<size_t>(seq) * kg.max_pages + pos / kg.page_tokens];
+    if (page < 0 || page >= kg.num_pages) return -1;
+    off = pos % kg.page_tokens;
+  }
+  return ((static_cast<long long>(page) * kg.num_layers + layer) * NKV + g) * kg.page_tokens + off;
+}
+
 // ------------------------------------------------------------ input RMSNorm
 // xn = half(h * (inv * w)), inv = rsqrtf(sum(h^2) / 1024 + eps) (megakernel.cu:806-847).
 // Layer 0 gathers h = embed[token] and stores it as the row's hidden state.
@@ -138,18 +159,21 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
     const __half *__restrict__ k_norm, const __half *__restrict__ cos_t,
     const __half *__restrict__ sin_t, const int *__restrict__ seq_ids,
     const int *__restrict__ positions, __half *__restrict__ k_pool, __half *__restrict__ v_pool,
-    __half *__restrict__ q_rot, int layer, int num_layers, int max_seq, int num_seqs,
+    __half *__restrict__ q_rot, int layer, KvGeom kg, int max_seq, int num_seqs,
     unsigned long long *err) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
   const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = positions[row];
   const int seq_id = seq_ids[row];
-  if (seq_id < 0 || seq_id >= num_seqs || pos < 0 || pos >= max_seq) {  // no cache access
+  // Out-of-range sequence or position, or an unmapped page: no cache access.
+  const long long row0 = (seq_id < 0 || seq_id >= num_seqs || pos < 0 || pos >= max_seq)
+                             ? -1 : kv_row(kg, seq_id, layer, 0, pos);
+  if (row0 < 0) {
     if (threadIdx.x == 0) record_err(err, 3);
     return;
   }
-  const size_t seq = static_cast<size_t>(seq_id);
+  const size_t head_stride = static_cast<size_t>(kg.page_tokens) * HD;  // kv head g -> g+1 in the pool
   const __half *src_row = qkv + static_cast<size_t>(row) * QKV;
   const __half *cosp = cos_t + static_cast<size_t>(pos) * HD;
   const __half *sinp = sin_t + static_cast<size_t>(pos) * HD;
@@ -169,7 +193,7 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
 #pragma unroll
     for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), __half2float(nw[lane + 32 * it]));
     __half *dst = is_q ? q_rot + static_cast<size_t>(row) * QS + hh * HD
-                       : k_pool + (((seq * num_layers + layer) * NKV + (hh - NQ)) * max_seq + pos) * HD;
+                       : k_pool + static_cast<size_t>(row0) * HD + (hh - NQ) * head_stride;
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
       const int i = lane + 32 * it;
@@ -183,7 +207,7 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
   // V (raw) into the cache: thread t copies elements 4t .. 4t+3.
   const int e = 4 * threadIdx.x, g = e / HD, d = e % HD;
   const uint2 val = *reinterpret_cast<const uint2 *>(src_row + QS + KVS + e);
-  *reinterpret_cast<uint2 *>(v_pool + (((seq * num_layers + layer) * NKV + g) * max_seq + pos) * HD + d) = val;
+  *reinterpret_cast<uint2 *>(v_pool + static_cast<size_t>(row0) * HD + g * head_stride + d) = val;
 }
 
 // ---------------------------------------------------------- split attention
@@ -222,7 +246,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __half *__restrict__ q_rot,
     const __half *__restrict__ k_pool,
     const __half *__restrict__ v_pool, const int *__restrict__ seq_ids,
-    const int *__restrict__ positions, float *__restrict__ part, int layer, int num_layers,
+    const int *__restrict__ positions, float *__restrict__ part, int layer, KvGeom kg,
     int max_seq, int max_splits, int num_seqs, float attn_scale, unsigned long long *err) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
@@ -237,8 +261,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   // 1024-byte aligned base: the swizzled K halves need it.
   AttnSmem &sm = *reinterpret_cast<AttnSmem *>(smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const size_t seq = static_cast<size_t>(seq_id);
-  const size_t krow0 = ((seq * num_layers + layer) * NKV + g) * max_seq + t0;  // row of K in the pool
+  // Row of the split's first K in the pool (a split never crosses a page:
+  // paged pools use pages of CH tokens and splits start at multiples of CH).
+  const long long krow_s = kv_row(kg, seq_id, layer, g, t0);
+  float *pp_out = part + ((static_cast<size_t>(row) * NKV + g) * max_splits + j) * 2 * PART;
+  if (krow_s < 0) {  // unmapped page: recorded, the split contributes nothing
+    if (tid == 0) record_err(err, 3);
+    if (tid < 2) {
+      pp_out[tid * PART + HD] = -INFINITY;
+      pp_out[tid * PART + HD + 1] = 0.f;
+    }
+    return;
+  }
+  const size_t krow0 = static_cast<size_t>(krow_s);
   const size_t base = krow0 * HD;
   if (tid == 0) {
     mbar_init(&sm.bar_k, 1);
@@ -543,8 +578,9 @@ struct Plan {
   const __half *embed, *final_norm, *cos_t, *sin_t;
   __half *k_pool, *v_pool;
   Workspace ws;
+  KvGeom kg;
   GemmPlan g_qkv[64], g_o[64], g_gu[64], g_down[64], g_lm;
-  CUtensorMap tm_k;   // K pool as [num_seqs * layers * 8 * max_seq rows, 128], 64 x CH boxes, 128B swizzle
+  CUtensorMap tm_k;   // K pool as [pages * layers * 8 * page_tokens rows, 128], 64 x CH boxes, 128B swizzle
 };
 
 int lm_tiles_for(int max_rows) {
@@ -562,16 +598,23 @@ long long qwen_b200_batched_workspace(int max_rows, int max_seq) {
   return static_cast<long long>(carve(nullptr, max_rows, max_splits, lm_tiles_for(max_rows), nullptr));
 }
 
-int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int num_layers,
-                             const void *embed, const void *final_norm, const void *cos_table,
-                             const void *sin_table, void *k_pool, void *v_pool, int num_seqs,
-                             int max_seq, int max_rows, void *workspace, long long workspace_bytes) {
+}  // extern "C"
+
+namespace {
+
+int create_plan(void **handle, const QwenBatchedLayer *layers, int num_layers, const void *embed,
+                const void *final_norm, const void *cos_table, const void *sin_table, void *k_pool,
+                void *v_pool, int num_seqs, int max_seq, int max_rows, void *workspace,
+                long long workspace_bytes, const int *page_table, int num_pages, int max_pages) {
   qb200_clear_error();
   if (handle == nullptr || layers == nullptr) return fail(13, "null pointer argument");
   *handle = nullptr;
   if (num_layers < 1 || num_layers > 64) return fail(10, "num_layers=%d out of range [1, 64]", num_layers);
   if (num_seqs < 1 || max_seq < 1 || max_seq > 65536 || max_rows < 1 || max_rows > 65535 * 8)
     return fail(10, "num_seqs=%d max_seq=%d max_rows=%d out of range", num_seqs, max_seq, max_rows);
+  if (page_table != nullptr && (num_pages < 1 || max_pages < 1 || static_cast<long long>(max_pages) * CH < max_seq))
+    return fail(10, "paged pools: num_pages=%d, max_pages=%d pages of %d tokens must cover max_seq=%d",
+                num_pages, max_pages, CH, max_seq);
   for (const void *p : {embed, final_norm, cos_table, sin_table, static_cast<const void *>(k_pool),
                         static_cast<const void *>(v_pool), static_cast<const void *>(workspace)})
     if (p == nullptr || !al16(p)) return fail(14, "pointers must be non-null and 16-byte aligned");
@@ -599,6 +642,11 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
   p->sin_t = static_cast<const __half *>(sin_table);
   p->k_pool = static_cast<__half *>(k_pool);
   p->v_pool = static_cast<__half *>(v_pool);
+  p->kg.page_table = page_table;
+  p->kg.num_layers = num_layers;
+  p->kg.max_pages = page_table != nullptr ? max_pages : 1;
+  p->kg.num_pages = page_table != nullptr ? num_pages : num_seqs;
+  p->kg.page_tokens = page_table != nullptr ? CH : max_seq;
   carve(static_cast<uint8_t *>(workspace), max_rows, p->max_splits, p->lm_tiles, &p->ws);
   int rc = 0;
   for (int l = 0; l < num_layers && rc == 0; ++l) {
@@ -609,7 +657,7 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
     if (!rc) rc = qb200_gemm_make_maps(&p->g_down[l], p->ws.inter, L.w_down, max_rows, H, IM, IM, IM);
   }
   if (!rc) rc = qb200_gemm_make_maps(&p->g_lm, p->ws.norm16, embed, max_rows, VOCAB, H, H, H);
-  const long long k_rows = static_cast<long long>(num_seqs) * num_layers * NKV * max_seq;
+  const long long k_rows = static_cast<long long>(p->kg.num_pages) * num_layers * NKV * p->kg.page_tokens;
   if (!rc && k_rows > 0x7fffffffll) rc = fail(10, "KV pool of %lld rows exceeds the tensor-map range", k_rows);
   if (!rc) rc = qb200_encode_f16_2d(&p->tm_k, k_pool, HD, k_rows, HD, HD / 2, CH, 1);
   if (rc) {
@@ -625,6 +673,33 @@ int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int 
   }
   *handle = p;
   return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_b200_batched_create(void **handle, const QwenBatchedLayer *layers, int num_layers,
+                             const void *embed, const void *final_norm, const void *cos_table,
+                             const void *sin_table, void *k_pool, void *v_pool, int num_seqs,
+                             int max_seq, int max_rows, void *workspace, long long workspace_bytes) {
+  return create_plan(handle, layers, num_layers, embed, final_norm, cos_table, sin_table, k_pool, v_pool,
+                     num_seqs, max_seq, max_rows, workspace, workspace_bytes, nullptr, 0, 0);
+}
+
+int qwen_b200_batched_create_paged(void **handle, const QwenBatchedLayer *layers, int num_layers,
+                                   const void *embed, const void *final_norm, const void *cos_table,
+                                   const void *sin_table, void *k_pool, void *v_pool, int num_pages,
+                                   const int *page_table, int max_pages_per_seq, int num_seqs,
+                                   int max_seq, int max_rows, void *workspace,
+                                   long long workspace_bytes) {
+  if (page_table == nullptr) {
+    qb200_clear_error();
+    return fail(13, "null page table");
+  }
+  return create_plan(handle, layers, num_layers, embed, final_norm, cos_table, sin_table, k_pool, v_pool,
+                     num_seqs, max_seq, max_rows, workspace, workspace_bytes, page_table, num_pages,
+                     max_pages_per_seq);
 }
 
 }  // extern "C"
@@ -660,11 +735,11 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     if (int rc = qb200_gemm_run(p->g_qkv[l], qb200tc::EPI_F16, g, st)) return rc;
     LAUNCH(qk_rope_kv_kernel, dim3(rows), dim3(256), 0, static_cast<const __half *>(w.qkv),
            static_cast<const __half *>(L.q_norm), static_cast<const __half *>(L.k_norm), p->cos_t,
-           p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->num_layers, p->max_seq,
+           p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->kg, p->max_seq,
            p->num_seqs, w.err);
     LAUNCH(attn_split_kernel, dim3(nsplit, NKV, rows), dim3(ATT_THREADS), smem, p->tm_k,
            static_cast<const __half *>(w.qrot), static_cast<const __half *>(p->k_pool),
-           static_cast<const __half *>(p->v_pool), seq_ids, positions, w.part, l, p->num_layers,
+           static_cast<const __half *>(p->v_pool), seq_ids, positions, w.part, l, p->kg,
            p->max_seq, p->max_splits, p->num_seqs, attn_scale, w.err);
     LAUNCH(attn_combine_kernel, dim3(NQ, rows), dim3(HD), 0, static_cast<const float *>(w.part),
            positions, w.attn, p->max_splits);
