@@ -214,16 +214,21 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
 
     n = args.seqs
     w_cpu = synthetic_weights(seed=SEED, num_layers=args.layers)
-    bd = BatchedDecoder(w_cpu, num_seqs=n, max_rows=n, device=dev, num_layers=args.layers)
     g = torch.Generator().manual_seed(1000 + rank)
     lengths = torch.randint(32, 513, (n,), generator=g).tolist()
     prompts = [torch.randint(0, 151936, (ln,), generator=g).tolist() for ln in lengths]
+    total_steps = args.warmup + args.steps
+    num_pages = sum((ln + total_steps + 127) // 128 for ln in lengths) if args.paged else None
+    bd = BatchedDecoder(w_cpu, num_seqs=n, max_rows=n, device=dev, num_layers=args.layers,
+                        paged=args.paged, num_pages=num_pages)
+    kv_bytes = 2 * bd.k_pool.numel() * 2
     bd.prefill(prompts)
+    for i, ln in enumerate(lengths):
+        bd.reserve(i, ln - 1 + total_steps - 1)
     ids = torch.arange(n, dtype=torch.int32, device=dev)
     pos0 = torch.tensor([ln - 1 for ln in lengths], dtype=torch.int32, device=dev)
     tok0 = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
     start_max = max(lengths) - 1
-    total_steps = args.warmup + args.steps
     assert start_max + 2 * total_steps < 2048
 
     # Device-timed run: warm-up steps, then the timed steps, continuing the generation.
@@ -316,7 +321,10 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
                    "batch": n, "prompt_len": "uniform [32, 512]", "gen_steps": args.steps,
                    "layers": args.layers if args.layers != 28 else None,
                    "parallelism": f"sequence shards x{world}" if world > 1 else "single GPU",
-                   "l2": f"inputs larger than L2 ({avg_alg / 1e9:.1f} GB of weights + KV read per step); no flush"},
+                   "l2": f"inputs larger than L2 ({avg_alg / 1e9:.1f} GB of weights + KV read per step); no flush",
+                   "kv": (f"paged: {bd.num_pages} pages of 128 tokens, {kv_bytes / 1e9:.1f} GB "
+                          f"(contiguous pools: {2 * n * args.layers * 8 * 2048 * 128 * 2 / 1e9:.1f} GB)"
+                          if args.paged else f"contiguous per-sequence pools, {kv_bytes / 1e9:.1f} GB")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
                      "algorithmic_bytes_per_step": avg_alg, "avg_step_ms": avg_step_s * 1000.0},
@@ -642,6 +650,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=256, help="rows per step (ops, lmhead workloads)")
     ap.add_argument("--layers", type=int, default=28,
                     help="model depth of the batched workload; fewer layers only for profiling captures")
+    ap.add_argument("--paged", action="store_true",
+                    help="batched workload: paged KV pools (128-token pages) instead of contiguous ones")
     ap.add_argument("--sampled", action="store_true",
                     help="decode workload: sample (temperature 0.8, top-k 50, top-p 0.9) instead of greedy")
     ap.add_argument("--profile", action="store_true",
