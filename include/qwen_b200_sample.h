@@ -47,6 +47,14 @@ int qwen_b200_sample(const float *logits, long long ld, int rows, int vocab, flo
                      const int *row_seq, const int *row_pos, int *out_tokens, float *kept_min,
                      void *stream);
 
+/* Path choice: with the default (1), calls of at most 96 rows of at most
+ * 8 x 19,200 logits hold each row in the shared memory of a cluster of 8 CTAs
+ * (read once, the selection run on the elements of a window that provably
+ * contains the kept set); other calls use one CTA per row; 0 forces one CTA
+ * per row.  Both give the same kept set and
+ * the same draws.  Process-wide; for tests and measurements. */
+void qwen_b200_sample_set_cluster(int enable);
+
 #ifdef __cplusplus
 }
 #endif

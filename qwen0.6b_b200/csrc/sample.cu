@@ -10,6 +10,7 @@
 // Level 0 reads the row; the elements of the boundary bin are collected into
 // shared memory (when they fit) and levels 1-2 run there, otherwise they read
 // the row again with the bin's prefix as a filter.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -324,10 +325,19 @@ __device__ uint32_t select_key(SampleSmem &s, const SampleArgs &a, const float *
   return prefix;
 }
 
-__global__ void __launch_bounds__(NT, 1) sample_kernel(SampleArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  SampleSmem &s = *reinterpret_cast<SampleSmem *>(smem_raw);
-  const int row = blockIdx.x, tid = threadIdx.x;
+// Random stream of a row: (row or row_seq[row], offset + row_pos[row]).
+__device__ __forceinline__ uint4 row_draw(const SampleArgs &a, int row, uint32_t group) {
+  const uint32_t stream_id = static_cast<uint32_t>(a.row_seq != nullptr ? a.row_seq[row] : row);
+  const uint32_t stream_pos = static_cast<uint32_t>(a.row_pos != nullptr ? a.row_pos[row] : 0);
+  return philox(make_uint4(group, stream_id, a.off_lo + stream_pos, a.off_hi), a.seed_lo, a.seed_hi);
+}
+__device__ __forceinline__ uint32_t word(const uint4 r, int j) {
+  return j == 0 ? r.x : (j == 1 ? r.y : (j == 2 ? r.z : r.w));
+}
+
+// One row by one CTA, reading the row from global memory for every pass.
+__device__ void sample_row(SampleSmem &s, const SampleArgs &a, int row) {
+  const int tid = threadIdx.x;
   const float *lg = a.logits + static_cast<size_t>(row) * a.ld;
   const int V = a.vocab;
 
@@ -366,15 +376,11 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(SampleArgs a) {
                                  [&](float z) { return expf(z - zmax); });
   }
 
-  // Gumbel-max over the kept set.  Stream of the row: (row or row_seq[row],
-  // offset + row_pos[row]).
-  const uint32_t stream_id = static_cast<uint32_t>(a.row_seq != nullptr ? a.row_seq[row] : row);
-  const uint32_t stream_pos = static_cast<uint32_t>(a.row_pos != nullptr ? a.row_pos[row] : 0);
+  // Gumbel-max over the kept set.
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   for (int g = tid; 4 * g < V; g += NT) {
-    const uint4 r = philox(make_uint4(static_cast<uint32_t>(g), stream_id, a.off_lo + stream_pos, a.off_hi),
-                           a.seed_lo, a.seed_hi);
+    const uint4 r = row_draw(a, row, static_cast<uint32_t>(g));
     const uint32_t rv[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -388,11 +394,269 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(SampleArgs a) {
   const int tok = block_argmax(s, bv, bi);
   if (tid == 0) {
     a.out[row] = tok;
-    if (a.kept_min != nullptr) a.kept_min[row] = kval(floor_key);
+    if (a.kept_min != nullptr) a.kept_min[row] = floor_key == 0u ? -INFINITY : kval(floor_key);
+  }
+}
+
+__global__ void __launch_bounds__(NT, 1) sample_kernel(SampleArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  sample_row(*reinterpret_cast<SampleSmem *>(smem_raw), a, blockIdx.x);
+}
+
+// ------------------------------------------------------ cluster-per-row path
+// A cluster of CL CTAs holds one row in shared memory (a slice of at most
+// SLICE elements per CTA, read from global memory once).  The CTAs publish
+// per-slice statistics (max, and for a ladder of windows [zmax - D, zmax]
+// the element count and softmax mass); every CTA derives the same smallest
+// window that must contain the kept set (top-k: at least k elements; top-p
+// alone: at least top_p of the total mass), collects its window elements, and
+// rank 0 gathers them through distributed shared memory and runs the exact
+// selection and the draw on that list.  The kept set, the random stream and
+// hence the token are those of the one-CTA path.  A row whose window would
+// not fit the list falls back to the one-CTA path on rank 0.
+constexpr int CL = 8;
+constexpr int SLICE = 19200;
+constexpr int NJ = 8;  // window ladder: D = 0.5 * 2^j (j < NJ - 1), then everything
+__device__ __forceinline__ float window_d(int j) { return j < NJ - 1 ? 0.5f * static_cast<float>(1 << j) : INFINITY; }
+
+struct ClusterSmem {
+  SampleSmem hs;       // histograms; hs.cand_key / hs.cand_w double as the list's key and z
+  int ci[CAP];         // the list's element indices
+  float zs[SLICE];     // this CTA's slice of z
+  float st_max, st_min, st_val;
+  int st_idx;
+  uint32_t st_cnt[NJ];
+  float st_mass[NJ];
+  float st_Z;
+  uint32_t st_n;       // window elements collected by this CTA
+  float zmax;
+  int jsel;
+  uint32_t red_u[NW];
+};
+
+template <bool MASS>
+__device__ uint32_t list_select(ClusterSmem &c, int n, uint32_t floor_key, float target_f, uint32_t target_u,
+                                float zmax) {
+  SampleSmem &s = c.hs;
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0;
+  for (int level = 0; level < 3; ++level) {
+    const int nb = nbins(level);
+    for (int b = tid; b < nb; b += NT) {
+      s.cnt[b] = 0u;
+      s.mass[b] = 0.f;
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t key = s.cand_key[i];
+      if (key >= floor_key && above(key, level) == prefix) {
+        const uint32_t d = digit(key, level);
+        atomicAdd(&s.cnt[d], 1u);
+        if (MASS) atomicAdd(&s.mass[d], expf(s.cand_w[i] - zmax));
+      }
+    }
+    __syncthreads();
+    const int bin = find_bin<MASS>(s, nb, target_f, target_u);
+    if (bin < 0) return floor_key;
+    target_f -= s.before_f;
+    target_u -= s.before_u;
+    prefix = compose(prefix, level, static_cast<uint32_t>(bin));
+  }
+  return prefix;
+}
+
+__global__ void __launch_bounds__(NT, 1) sample_cluster_kernel(SampleArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  ClusterSmem &c = *reinterpret_cast<ClusterSmem *>(smem_raw);
+  const int rank = static_cast<int>(cluster.block_rank()), row = blockIdx.y, tid = threadIdx.x;
+  const int V = a.vocab;
+  const int slice = ((V + CL - 1) / CL + 3) & ~3;  // multiple of 4: draw groups stay in one CTA
+  const int lo = min(V, rank * slice), n = min(V, lo + slice) - lo;
+  const float *lg = a.logits + static_cast<size_t>(row) * a.ld + lo;
+  const bool greedy = a.temperature <= 0.f || a.top_k == 1;
+  float mx = -INFINITY, mn = INFINITY, bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < n; i += NT) {
+    const float z = greedy ? lg[i] : __fdiv_rn(lg[i], a.temperature);
+    c.zs[i] = z;
+    mx = fmaxf(mx, z);
+    mn = fminf(mn, z);
+    if (greedy) better(bv, bi, z, lo + i);
+  }
+  mx = block_max(c.hs, mx);
+  mn = -block_max(c.hs, -mn);
+  const bool all = !greedy && (a.top_k == 0 || a.top_k >= V) && a.top_p >= 1.f;
+  if (all) {  // temperature only: Gumbel-max over the whole slice
+    for (int g = tid; 4 * g < n; g += NT) {
+      const uint4 r = row_draw(a, row, static_cast<uint32_t>((lo >> 2) + g));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = 4 * g + j;
+        if (i < n) better(bv, bi, c.zs[i] + gumbel(word(r, j)), lo + i);
+      }
+    }
+  }
+  if (greedy || all) {
+    const int idx = block_argmax(c.hs, bv, bi);
+    if (tid == 0) {
+      // The winner's score, recomputed from its index (same arithmetic as above).
+      float v = -INFINITY;
+      if (idx >= lo && idx < lo + n)
+        v = greedy ? c.zs[idx - lo]
+                   : c.zs[idx - lo] + gumbel(word(row_draw(a, row, static_cast<uint32_t>(idx >> 2)), idx & 3));
+      c.st_val = v;
+      c.st_idx = idx;
+      c.st_min = mn;
+    }
+    cluster.sync();
+    if (rank == 0 && tid == 0) {
+      float best = -INFINITY, lowest = INFINITY;
+      int bidx = 0x7fffffff;
+      for (int r = 0; r < CL; ++r) {
+        ClusterSmem *o = cluster.map_shared_rank(&c, r);
+        better(best, bidx, o->st_val, o->st_idx);
+        lowest = fminf(lowest, o->st_min);
+      }
+      a.out[row] = bidx;
+      if (a.kept_min != nullptr) a.kept_min[row] = greedy ? best : lowest;
+    }
+    cluster.sync();
+    return;
+  }
+  // Window statistics of this slice.
+  if (tid == 0) c.st_max = mx;
+  cluster.sync();
+  if (tid == 0) {
+    float zm = -INFINITY;
+    for (int r = 0; r < CL; ++r) zm = fmaxf(zm, cluster.map_shared_rank(&c, r)->st_max);
+    c.zmax = zm;
+  }
+  __syncthreads();
+  const float zmax = c.zmax;
+  uint32_t cnt[NJ];
+  float mass[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    cnt[j] = 0u;
+    mass[j] = 0.f;
+  }
+  for (int i = tid; i < n; i += NT) {
+    const float d = zmax - c.zs[i];
+    const float w = expf(-d);
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      if (d <= window_d(j)) {
+        ++cnt[j];
+        mass[j] += w;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    const float m = block_sum(c.hs, mass[j]);
+    uint32_t u = cnt[j];
+    for (int o = 16; o > 0; o >>= 1) u += __shfl_xor_sync(0xffffffffu, u, o);
+    if ((tid & 31) == 0) c.red_u[tid >> 5] = u;
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < NW; ++w) t += c.red_u[w];
+      c.st_cnt[j] = t;
+      c.st_mass[j] = m;
+    }
+    __syncthreads();
+  }
+  cluster.sync();
+  const bool use_k = a.top_k > 0 && a.top_k < V;
+  const bool use_p = a.top_p < 1.f;
+  if (tid == 0) {
+    int js = -1;
+    float Zt = 0.f;
+    for (int r = 0; r < CL; ++r) Zt += cluster.map_shared_rank(&c, r)->st_mass[NJ - 1];
+    for (int j = 0; j < NJ && js < 0; ++j) {
+      uint32_t ct = 0;
+      float mt = 0.f;
+      for (int r = 0; r < CL; ++r) {
+        ClusterSmem *o = cluster.map_shared_rank(&c, r);
+        ct += o->st_cnt[j];
+        mt += o->st_mass[j];
+      }
+      const bool ok = (use_k ? ct >= static_cast<uint32_t>(a.top_k) : (!use_p || mt >= a.top_p * Zt)) &&
+                      ct <= static_cast<uint32_t>(CAP);
+      if (ok) js = j;
+    }
+    c.jsel = js;
+    c.st_Z = Zt;
+  }
+  __syncthreads();
+  const int js = c.jsel;
+  if (js < 0) {  // window does not fit the list: the one-CTA path on rank 0
+    cluster.sync();
+    if (rank == 0) sample_row(c.hs, a, row);
+    return;
+  }
+  // Collect this slice's window elements.
+  if (tid == 0) c.st_n = 0u;
+  __syncthreads();
+  const float dsel = window_d(js);
+  for (int i = tid; i < n; i += NT) {
+    const float z = c.zs[i];
+    if (zmax - z <= dsel) {
+      const uint32_t slot = atomicAdd(&c.st_n, 1u);
+      c.hs.cand_key[slot] = fkey(z);
+      c.hs.cand_w[slot] = z;
+      c.ci[slot] = lo + i;
+    }
+  }
+  cluster.sync();
+  // Rank 0 appends the other ranks' lists to its own.
+  int total = 0;
+  if (rank == 0) {
+    total = static_cast<int>(c.st_n);
+    for (int r = 1; r < CL; ++r) {
+      ClusterSmem *o = cluster.map_shared_rank(&c, r);
+      const int m = static_cast<int>(o->st_n);
+      for (int i = tid; i < m; i += NT) {
+        c.hs.cand_key[total + i] = o->hs.cand_key[i];
+        c.hs.cand_w[total + i] = o->hs.cand_w[i];
+        c.ci[total + i] = o->ci[i];
+      }
+      total += m;
+    }
+  }
+  cluster.sync();  // the other ranks' shared memory is no longer read
+  if (rank != 0) return;
+  uint32_t floor_key = 0u;
+  if (use_k) floor_key = list_select<false>(c, total, 0u, 0.f, static_cast<uint32_t>(a.top_k), zmax);
+  if (use_p) {
+    float Z = c.st_Z;
+    if (use_k) {
+      float part = 0.f;
+      for (int i = tid; i < total; i += NT)
+        if (c.hs.cand_key[i] >= floor_key) part += expf(c.hs.cand_w[i] - zmax);
+      Z = block_sum(c.hs, part);
+    }
+    floor_key = list_select<true>(c, total, floor_key, a.top_p * Z, 0u, zmax);
+  }
+  bv = -INFINITY;
+  bi = 0x7fffffff;
+  for (int i = tid; i < total; i += NT) {
+    if (c.hs.cand_key[i] >= floor_key) {
+      const int idx = c.ci[i];
+      better(bv, bi, c.hs.cand_w[i] + gumbel(word(row_draw(a, row, static_cast<uint32_t>(idx >> 2)), idx & 3)), idx);
+    }
+  }
+  const int tok = block_argmax(c.hs, bv, bi);
+  if (tid == 0) {
+    a.out[row] = tok;
+    if (a.kept_min != nullptr) a.kept_min[row] = floor_key == 0u ? -INFINITY : kval(floor_key);
   }
 }
 
 int g_attr_done[64];
+int g_cluster_ok[64];  // 0 unknown, 1 usable, -1 not
 
 }  // namespace
 
@@ -440,11 +704,60 @@ extern "C" int qwen_b200_sample(const float *logits, long long ld, int rows, int
   a.row_pos = row_pos;
   a.out = out_tokens;
   a.kept_min = kept_min;
-  sample_kernel<<<rows, NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  // Cluster-per-row path when the row fits CL slices, clusters of CL such CTAs
+  // can be co-scheduled on this device and the rows are few; else one CTA per row.
+  const int slice = ((vocab + CL - 1) / CL + 3) & ~3;
+  if (slice <= SLICE && g_cluster_ok[dev] == 0) {
+    const int csmem = static_cast<int>(sizeof(ClusterSmem));
+    cudaError_t ce = cudaFuncSetAttribute(sample_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, csmem);
+    int nclusters = 0;
+    if (ce == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(CL, 1, 1);
+      cfg.blockDim = dim3(NT, 1, 1);
+      cfg.dynamicSmemBytes = csmem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = CL;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      ce = cudaOccupancyMaxActiveClusters(&nclusters, sample_cluster_kernel, &cfg);
+    }
+    g_cluster_ok[dev] = (ce == cudaSuccess && nclusters > 0) ? 1 : -1;
+    cudaGetLastError();  // a refused probe leaves no sticky error
+  }
+  cudaError_t e;
+  // 18 clusters of 8 run at a time on 148 SMs and one takes ~35 us, while the
+  // one-CTA path runs 148 rows at a time in ~200 us: clusters up to ~100 rows.
+  if (slice <= SLICE && g_cluster_ok[dev] == 1 && rows <= 96) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL, static_cast<unsigned>(rows), 1);
+    cfg.blockDim = dim3(NT, 1, 1);
+    cfg.dynamicSmemBytes = sizeof(ClusterSmem);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CL;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, sample_cluster_kernel, a);
+  } else {
+    sample_kernel<<<rows, NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     snprintf(msg, sizeof msg, "sample kernel launch: %s", cudaGetErrorString(e));
     return qb200_set_error(41, msg);
   }
   return 0;
+}
+
+extern "C" void qwen_b200_sample_set_cluster(int enable) {
+  for (int d = 0; d < 64; ++d)
+    if (!enable) g_cluster_ok[d] = -1;
+    else if (g_cluster_ok[d] == -1) g_cluster_ok[d] = 0;
 }

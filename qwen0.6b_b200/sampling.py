@@ -37,6 +37,8 @@ def lib() -> ctypes.CDLL:
         vp, i, ll, ull, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_ulonglong, ctypes.c_float
         L.qwen_b200_sample.restype = i
         L.qwen_b200_sample.argtypes = [vp, ll, i, i, f, i, f, ull, ull, vp, vp, vp, vp, vp]
+        L.qwen_b200_sample_set_cluster.restype = None
+        L.qwen_b200_sample_set_cluster.argtypes = [i]
         L.qwen_b200_last_error.restype = i
         L.qwen_b200_last_error.argtypes = [ctypes.c_char_p, i]
         _lib = L
@@ -48,6 +50,11 @@ def _check(rc: int, what: str) -> None:
         buf = ctypes.create_string_buffer(512)
         lib().qwen_b200_last_error(buf, 512)
         raise RuntimeError(f"{what} failed (code {rc}): {buf.value.decode()}")
+
+
+def set_cluster_path(enable: bool) -> None:
+    """Cluster-of-8-CTAs-per-row path (default) or one CTA per row (same results)."""
+    lib().qwen_b200_sample_set_cluster(1 if enable else 0)
 
 
 def sample(logits: torch.Tensor, params: SamplingParams, offset: int = 0,

@@ -146,6 +146,31 @@ def test_radix_overflow_path():
     assert float(km[0]) == 0.0                                 # all kept, as TopKLogitsWarper keeps ties
 
 
+@pytest.mark.parametrize("T,k,p", [(1.0, 50, 1.0), (0.8, 200, 0.9), (1.0, 0, 0.7), (1.3, 0, 1.0),
+                                   (0.0, 0, 1.0), (1.0, 1, 1.0)])
+def test_cluster_and_one_cta_paths_agree(T, k, p):
+    """The cluster-per-row path (a window that contains the kept set, held in
+    shared memory) and the one-CTA path give the same kept set and tokens."""
+    from sampling import set_cluster_path
+    g = torch.Generator(device="cuda").manual_seed(77 + k)
+    logits = 3.0 * torch.randn(5, V, generator=g, device="cuda")
+    try:
+        set_cluster_path(True)
+        t_c, km_c = run(logits, T, k, p, seed=9, offset=3)
+        set_cluster_path(False)
+        t_1, km_1 = run(logits, T, k, p, seed=9, offset=3)
+    finally:
+        set_cluster_path(True)
+    if p >= 1.0 and T > 0 and k not in (0, 1):
+        assert torch.equal(km_c, km_1)                         # exact thresholds
+    z = logits.cpu() / T if T > 0 else logits.cpu()
+    for r in range(5):
+        d = int(((z[r] >= km_c[r]) != (z[r] >= km_1[r])).sum())
+        assert d <= 2, (r, d)                                  # top-p: fp32 mass order only
+        if d == 0:
+            assert int(t_c[r]) == int(t_1[r])                  # same set, same noise, same token
+
+
 def test_rejects_bad_parameters():
     from sampling import SamplingParams, sample
     x = torch.zeros(1, 10, device="cuda")
