@@ -29,8 +29,11 @@ extern "C" {
  *   5  out int32 [M]      = column of the row maximum of C (lowest on ties);
  *                           workspace of qwen_b200_gemm_argmax_workspace bytes
  * k_splits > 1 (epilogues 0, 1, 2, 4) cuts K into that many slices computed by
- * separate CTAs into fp32 partials (workspace of k_splits * M * N * 4 bytes),
- * summed in slice order before the epilogue.
+ * separate CTAs and summed in slice order before the epilogue: with a
+ * workspace (k_splits * M * N * 4 bytes) through fp32 partials in global
+ * memory and a reduction kernel; with workspace NULL (k_splits <= 8) inside a
+ * thread-block cluster of the k_splits CTAs of a tile (partial tiles added
+ * through distributed shared memory, one launch).  Both give the same bits.
  * Requirements: N a multiple of 16, K a multiple of 64, 16-byte aligned
  * pointers.
  */

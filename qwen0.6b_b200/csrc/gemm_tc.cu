@@ -185,8 +185,9 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, cu
   GemmArgs ga = g;
   const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
   ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
-  const cudaError_t e = qb200_launch(gemm_tc_kernel<BN, EPI>, grid, dim3(THREADS),
-                                     GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0, ma, mb, ga);
+  const cudaError_t e = qb200_launch_cl(gemm_tc_kernel<BN, EPI>, grid, dim3(THREADS),
+                                        GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0,
+                                        ga.cluster_k ? static_cast<int>(grid.z) : 1, ma, mb, ga);
   if (e != cudaSuccess) return fail(20, "GEMM launch: %s", cudaGetErrorString(e));
   return 0;
 }
@@ -245,6 +246,13 @@ int qb200_gemm_run_splitk(const GemmPlan &p, int epi, GemmArgs g, int splits, fl
   if (splits < 2 || splits > nk) return fail(10, "k_splits=%d out of range [2, %d]", splits, nk);
   if (epi != EPI_F16 && epi != EPI_F32 && epi != EPI_F32_RES16 && epi != EPI_F16_RES32)
     return fail(10, "epilogue %d cannot follow a split-K reduction", epi);
+  if (splits <= 8 && partial == nullptr) {
+    // The k slices of a tile form one cluster and are added in shared memory.
+    GemmArgs gc = g;
+    gc.k_splits = splits;
+    gc.cluster_k = 1;
+    return qb200_gemm_run(p, epi, gc, st);
+  }
   GemmArgs gp = g;
   gp.out = partial;
   gp.ldo = p.N;
@@ -327,8 +335,8 @@ int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, co
   if (epilogue < 0 || epilogue > EPI_ARGMAX) return fail(10, "unknown epilogue %d", epilogue);
   if ((epilogue == EPI_F32_RES16 || epilogue == EPI_F16_RES32) && res == nullptr)
     return fail(13, "this epilogue needs a residual");
-  if ((epilogue == EPI_ARGMAX || k_splits > 1) && workspace == nullptr)
-    return fail(13, "argmax and split-K need a workspace");
+  if (epilogue == EPI_ARGMAX && workspace == nullptr) return fail(13, "argmax needs a workspace");
+  if (k_splits > 8 && workspace == nullptr) return fail(13, "more than 8 k slices need a workspace");
   GemmPlan p{};
   if (int rc = qb200_gemm_make_maps(&p, a, b, M, N, K, K, K)) return rc;
   GemmArgs g{};

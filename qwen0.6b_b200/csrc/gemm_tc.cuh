@@ -65,6 +65,7 @@ struct GemmArgs {
   int n_tiles;
   int k_splits;                 // grid.z: the K range is cut into this many slices (EPI_PARTIAL)
   int stages;                   // ring depth of this launch (<= max_stages<BN>())
+  int cluster_k;                // split-K reduced inside a (1, 1, k_splits) cluster (see below)
   int pdl;                      // host side: launch as a programmatic dependent of the previous kernel
   unsigned long long *err;      // status word (nullptr: none)
 };
@@ -157,6 +158,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 static __device__ __noinline__ void gemm_record(unsigned long long *err, uint32_t code) {
   if (err == nullptr) return;
   const unsigned long long v = (static_cast<unsigned long long>(code) << 32) |
@@ -214,6 +237,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Split-K reduced in the cluster (launched with cluster dims (1, 1, k_splits)).
+  constexpr bool CAN_CLUSTER = EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_F32_RES16 || EPI == EPI_F16_RES32;
+  const bool clustered = CAN_CLUSTER && g.cluster_k != 0 && gridDim.z > 1;
+  constexpr int TPITCH = BN + 4;  // fp32 partial tile row pitch (16-byte shift per row)
   const int nk_all = (g.K + BK - 1) / BK;
   // Split-K slice of this CTA (a single slice unless EPI_PARTIAL).
   const int kb0 = static_cast<int>((static_cast<long long>(nk_all) * blockIdx.z) / gridDim.z);
@@ -300,7 +327,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = gemm_wait(acc_full, 0, abort, g.err, 3);
     ok = __all_sync(0xffffffffu, ok && !*abort);  // tcgen05.ld below is warp-collective
     tc_fence_after();
-    if (ok) {
+    if (ok && clustered) {
+      // This k slice's partial tile into shared memory (the ring is idle:
+      // every copy has landed and every MMA has completed).
+      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      float *trow = reinterpret_cast<float *>(base) + (32 * q + lane) * TPITCH;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tq + c0, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4 *>(trow + c0)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    } else if (ok) {
       const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
       float best = -INFINITY;
       int best_i = 0x7fffffff;
@@ -372,6 +412,50 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (clustered) {
+    // Split-K reduced inside the cluster: rank 0 adds the k slices' partial
+    // tiles in slice order (as the separate reduction kernel adds its slices),
+    // then applies the epilogue.  Every thread of every CTA takes both
+    // cluster barriers, also after an abort.
+    cluster_sync_all();
+    if (cluster_rank() == 0 && warp >= 2) {
+      const int q = warp & 3, lrow = 32 * q + lane, row = m0 + lrow;
+      const uint32_t trow = smem_u32(base) + static_cast<uint32_t>(lrow * TPITCH) * 4u;
+      if (row < g.M && !*abort) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 4) {
+          const int col = n0 + c;
+          if (col >= g.N) break;
+          float4 acc = ld_dsmem_f4(map_rank(trow + c * 4, 0));
+          for (uint32_t z = 1; z < gridDim.z; ++z) {
+            const float4 v = ld_dsmem_f4(map_rank(trow + c * 4, z));
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+          }
+          const size_t o = static_cast<size_t>(row) * g.ldo + col;
+          if constexpr (EPI == EPI_F32_RES16) {
+            const __half *r = static_cast<const __half *>(g.res) + o;
+            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) =
+                make_float4(__fadd_rn(acc.x, __half2float(r[0])), __fadd_rn(acc.y, __half2float(r[1])),
+                            __fadd_rn(acc.z, __half2float(r[2])), __fadd_rn(acc.w, __half2float(r[3])));
+          } else if constexpr (EPI == EPI_F16_RES32) {
+            const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(g.res) + o);
+            __half2 h[2] = {__floats2half2_rn(__fadd_rn(acc.x, r.x), __fadd_rn(acc.y, r.y)),
+                            __floats2half2_rn(__fadd_rn(acc.z, r.z), __fadd_rn(acc.w, r.w))};
+            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+          } else if constexpr (EPI == EPI_F32) {
+            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) = acc;
+          } else if constexpr (EPI == EPI_F16) {
+            __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
+            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+          }
+        }
+      }
+    }
+    cluster_sync_all();  // the other ranks' tiles are no longer read
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);

@@ -154,6 +154,28 @@ def test_gemm_split_k(M, N, K, splits):
     assert torch.allclose(gemm(EPI_F32, a, b, k_splits=splits), ref, atol=1e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("M,N,K,splits", [(256, 1024, 2048, 4), (256, 1024, 3072, 4), (77, 1024, 3072, 3),
+                                          (5, 64, 128, 2)])
+def test_cluster_split_k_equals_workspace_split_k(M, N, K, splits):
+    """Split-K added inside a thread-block cluster (workspace NULL) gives the
+    same bits as the partials-in-global-memory path."""
+    f, _ = _fn()
+    a, b = _inputs(M, N, K, 23)
+    for epi, odt, rdt in ((EPI_F32_RES16, torch.float32, torch.float16), (EPI_F16_RES32, torch.float16, torch.float32),
+                          (EPI_F32, torch.float32, None), (EPI_F16, torch.float16, None)):
+        res = torch.randn(M, N, device="cuda").to(rdt) if rdt is not None else None
+        outs = []
+        for ws in (torch.empty(splits * M * N * 4, dtype=torch.uint8, device="cuda"), None):
+            out = torch.empty(M, N, dtype=odt, device="cuda")
+            rc = f(epi, a.data_ptr(), b.data_ptr(), out.data_ptr(), res.data_ptr() if res is not None else None,
+                   ws.data_ptr() if ws is not None else None, M, N, K, N, splits,
+                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert rc == 0, last_error()
+            torch.cuda.synchronize()
+            outs.append(out)
+        assert torch.equal(outs[0], outs[1]), epi
+
+
 def test_gemm_rejects_bad_shapes():
     f, _ = _fn()
     a = torch.zeros(4, 100, dtype=torch.float16, device="cuda")
