@@ -44,6 +44,7 @@ struct SampleSmem {
   float mass[NBIN];
   uint32_t cand_key[CAP];
   float cand_w[CAP];
+  int cand_i[CAP];  // element indices of a window list
   uint32_t n_cand;
   int found;
   float before_f;
@@ -335,6 +336,111 @@ __device__ __forceinline__ uint32_t word(const uint4 r, int j) {
   return j == 0 ? r.x : (j == 1 ? r.y : (j == 2 ? r.z : r.w));
 }
 
+__device__ __forceinline__ uint32_t block_sum_u(SampleSmem &s, uint32_t v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) s.red_i[threadIdx.x >> 5] = static_cast<int>(v);
+  __syncthreads();
+  uint32_t t = 0u;
+  for (int i = 0; i < NW; ++i) t += static_cast<uint32_t>(s.red_i[i]);
+  __syncthreads();
+  return t;
+}
+
+// Window pre-filter.  For a ladder of windows [zmax - D, zmax] the element
+// count and softmax mass are taken in one pass; the smallest window that must
+// contain the kept set (top-k: at least k elements, so every element of the
+// k-th largest key's group; top-p alone: at least top_p of the total mass) is
+// collected into a list of at most CAP elements, and the exact selections and
+// the draw run on that list.  The kept set is a prefix of the descending order,
+// and so is every window, which is why the selection on the list equals the
+// selection on the row.
+constexpr int NJ = 8;  // window ladder: D = 0.5 * 2^j (j < NJ - 1), then everything
+__device__ __forceinline__ float window_d(int j) { return j < NJ - 1 ? 0.5f * static_cast<float>(1 << j) : INFINITY; }
+
+// Smallest window index whose (count, mass) totals admit the kept set and
+// whose count fits the list, or -1.
+__device__ __forceinline__ int pick_window(const SampleArgs &a, const uint32_t *ct, const float *mt, float Zt) {
+  const bool use_k = a.top_k > 0 && a.top_k < a.vocab;
+  const bool use_p = a.top_p < 1.f;
+  for (int j = 0; j < NJ; ++j) {
+    const bool ok = (use_k ? ct[j] >= static_cast<uint32_t>(a.top_k) : (!use_p || mt[j] >= a.top_p * Zt)) &&
+                    ct[j] <= static_cast<uint32_t>(CAP);
+    if (ok && ct[j] > 0u) return j;
+  }
+  return -1;
+}
+
+// Exact radix selection (as select_key) over the n-element list in
+// s.cand_key / s.cand_w (z), restricted to keys >= floor_key.
+template <bool MASS>
+__device__ uint32_t list_select(SampleSmem &s, int n, uint32_t floor_key, float target_f, uint32_t target_u,
+                                float zmax) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0;
+  for (int level = 0; level < 3; ++level) {
+    const int nb = nbins(level);
+    for (int b = tid; b < nb; b += NT) {
+      s.cnt[b] = 0u;
+      s.mass[b] = 0.f;
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t key = s.cand_key[i];
+      if (key >= floor_key && above(key, level) == prefix) {
+        const uint32_t d = digit(key, level);
+        atomicAdd(&s.cnt[d], 1u);
+        if (MASS) atomicAdd(&s.mass[d], expf(s.cand_w[i] - zmax));
+      }
+    }
+    __syncthreads();
+    const int bin = find_bin<MASS>(s, nb, target_f, target_u);
+    if (bin < 0) return floor_key;
+    target_f -= s.before_f;
+    target_u -= s.before_u;
+    prefix = compose(prefix, level, static_cast<uint32_t>(bin));
+  }
+  return prefix;
+}
+
+// Top-k / top-p thresholds and the Gumbel-max draw on the n-element window
+// list (keys, z and indices in s); writes the token and kept_min.  Z_all is
+// the softmax mass of the whole row (used when top-k is off).
+__device__ void finish_list(SampleSmem &s, const SampleArgs &a, int row, int n, float zmax, float Z_all) {
+  const int tid = threadIdx.x;
+  const bool use_k = a.top_k > 0 && a.top_k < a.vocab;
+  const bool use_p = a.top_p < 1.f;
+  uint32_t floor_key = 0u;
+  if (use_k) floor_key = list_select<false>(s, n, 0u, 0.f, static_cast<uint32_t>(a.top_k), zmax);
+  if (use_p) {
+    float Z = Z_all;
+    if (use_k) {
+      float part = 0.f;
+      for (int i = tid; i < n; i += NT)
+        if (s.cand_key[i] >= floor_key) part += expf(s.cand_w[i] - zmax);
+      Z = block_sum(s, part);
+    }
+    floor_key = list_select<true>(s, n, floor_key, a.top_p * Z, 0u, zmax);
+  }
+  if (floor_key == 0u) {  // rounding left the top-p target unreached: the whole list is kept
+    float m = -INFINITY;
+    for (int i = tid; i < n; i += NT) m = fmaxf(m, -s.cand_w[i]);
+    floor_key = fkey(-block_max(s, m));
+  }
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < n; i += NT) {
+    if (s.cand_key[i] >= floor_key) {
+      const int idx = s.cand_i[i];
+      better(bv, bi, s.cand_w[i] + gumbel(word(row_draw(a, row, static_cast<uint32_t>(idx >> 2)), idx & 3)), idx);
+    }
+  }
+  const int tok = block_argmax(s, bv, bi);
+  if (tid == 0) {
+    a.out[row] = tok;
+    if (a.kept_min != nullptr) a.kept_min[row] = floor_key == 0u ? -INFINITY : kval(floor_key);
+  }
+}
+
 // One row by one CTA, reading the row from global memory for every pass.
 __device__ void sample_row(SampleSmem &s, const SampleArgs &a, int row) {
   const int tid = threadIdx.x;
@@ -358,10 +464,54 @@ __device__ void sample_row(SampleSmem &s, const SampleArgs &a, int row) {
   const bool use_p = a.top_p < 1.f;
   uint32_t floor_key = 0u;
   float zmax = -INFINITY;
-  if (use_p) {
+  if (use_k || use_p) {
     float m = -INFINITY;
     for_row(a, lg, [&](int, float z, uint32_t) { m = fmaxf(m, z); });
     zmax = block_max(s, m);
+    // Window pre-filter: one pass for the ladder's counts and masses, one to
+    // collect the chosen window; the selections then run on the list.
+    uint32_t cnt[NJ];
+    float mass[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      cnt[j] = 0u;
+      mass[j] = 0.f;
+    }
+    for_row(a, lg, [&](int, float z, uint32_t) {
+      const float d = zmax - z;
+      const float w = expf(-d);
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        if (d <= window_d(j)) {
+          ++cnt[j];
+          mass[j] += w;
+        }
+      }
+    });
+    uint32_t ct[NJ];
+    float mt[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      mt[j] = block_sum(s, mass[j]);
+      ct[j] = block_sum_u(s, cnt[j]);
+    }
+    const int js = pick_window(a, ct, mt, mt[NJ - 1]);
+    if (js >= 0) {
+      const float dsel = window_d(js);
+      if (tid == 0) s.n_cand = 0u;
+      __syncthreads();
+      for_row(a, lg, [&](int i, float z, uint32_t key) {
+        if (zmax - z <= dsel) {
+          const uint32_t slot = atomicAdd(&s.n_cand, 1u);
+          s.cand_key[slot] = key;
+          s.cand_w[slot] = z;
+          s.cand_i[slot] = i;
+        }
+      });
+      __syncthreads();
+      finish_list(s, a, row, static_cast<int>(s.n_cand), zmax, mt[NJ - 1]);
+      return;
+    }
   }
   if (use_k)
     floor_key = select_key<false>(s, a, lg, 0u, 0.f, static_cast<uint32_t>(a.top_k),
@@ -416,12 +566,9 @@ __global__ void __launch_bounds__(NT, 1) sample_kernel(SampleArgs a) {
 // not fit the list falls back to the one-CTA path on rank 0.
 constexpr int CL = 8;
 constexpr int SLICE = 19200;
-constexpr int NJ = 8;  // window ladder: D = 0.5 * 2^j (j < NJ - 1), then everything
-__device__ __forceinline__ float window_d(int j) { return j < NJ - 1 ? 0.5f * static_cast<float>(1 << j) : INFINITY; }
 
 struct ClusterSmem {
-  SampleSmem hs;       // histograms; hs.cand_key / hs.cand_w double as the list's key and z
-  int ci[CAP];         // the list's element indices
+  SampleSmem hs;       // histograms; hs.cand_key / cand_w / cand_i hold the list's key, z and index
   float zs[SLICE];     // this CTA's slice of z
   float st_max, st_min, st_val;
   int st_idx;
@@ -433,37 +580,6 @@ struct ClusterSmem {
   int jsel;
   uint32_t red_u[NW];
 };
-
-template <bool MASS>
-__device__ uint32_t list_select(ClusterSmem &c, int n, uint32_t floor_key, float target_f, uint32_t target_u,
-                                float zmax) {
-  SampleSmem &s = c.hs;
-  const int tid = threadIdx.x;
-  uint32_t prefix = 0;
-  for (int level = 0; level < 3; ++level) {
-    const int nb = nbins(level);
-    for (int b = tid; b < nb; b += NT) {
-      s.cnt[b] = 0u;
-      s.mass[b] = 0.f;
-    }
-    __syncthreads();
-    for (int i = tid; i < n; i += NT) {
-      const uint32_t key = s.cand_key[i];
-      if (key >= floor_key && above(key, level) == prefix) {
-        const uint32_t d = digit(key, level);
-        atomicAdd(&s.cnt[d], 1u);
-        if (MASS) atomicAdd(&s.mass[d], expf(s.cand_w[i] - zmax));
-      }
-    }
-    __syncthreads();
-    const int bin = find_bin<MASS>(s, nb, target_f, target_u);
-    if (bin < 0) return floor_key;
-    target_f -= s.before_f;
-    target_u -= s.before_u;
-    prefix = compose(prefix, level, static_cast<uint32_t>(bin));
-  }
-  return prefix;
-}
 
 __global__ void __launch_bounds__(NT, 1) sample_cluster_kernel(SampleArgs a) {
   namespace cg = cooperative_groups;
@@ -569,26 +685,20 @@ __global__ void __launch_bounds__(NT, 1) sample_cluster_kernel(SampleArgs a) {
     __syncthreads();
   }
   cluster.sync();
-  const bool use_k = a.top_k > 0 && a.top_k < V;
-  const bool use_p = a.top_p < 1.f;
   if (tid == 0) {
-    int js = -1;
-    float Zt = 0.f;
-    for (int r = 0; r < CL; ++r) Zt += cluster.map_shared_rank(&c, r)->st_mass[NJ - 1];
-    for (int j = 0; j < NJ && js < 0; ++j) {
-      uint32_t ct = 0;
-      float mt = 0.f;
+    uint32_t ct[NJ];
+    float mt[NJ];
+    for (int j = 0; j < NJ; ++j) {
+      ct[j] = 0u;
+      mt[j] = 0.f;
       for (int r = 0; r < CL; ++r) {
         ClusterSmem *o = cluster.map_shared_rank(&c, r);
-        ct += o->st_cnt[j];
-        mt += o->st_mass[j];
+        ct[j] += o->st_cnt[j];
+        mt[j] += o->st_mass[j];
       }
-      const bool ok = (use_k ? ct >= static_cast<uint32_t>(a.top_k) : (!use_p || mt >= a.top_p * Zt)) &&
-                      ct <= static_cast<uint32_t>(CAP);
-      if (ok) js = j;
     }
-    c.jsel = js;
-    c.st_Z = Zt;
+    c.jsel = pick_window(a, ct, mt, mt[NJ - 1]);
+    c.st_Z = mt[NJ - 1];
   }
   __syncthreads();
   const int js = c.jsel;
@@ -607,7 +717,7 @@ __global__ void __launch_bounds__(NT, 1) sample_cluster_kernel(SampleArgs a) {
       const uint32_t slot = atomicAdd(&c.st_n, 1u);
       c.hs.cand_key[slot] = fkey(z);
       c.hs.cand_w[slot] = z;
-      c.ci[slot] = lo + i;
+      c.hs.cand_i[slot] = lo + i;
     }
   }
   cluster.sync();
@@ -621,38 +731,14 @@ __global__ void __launch_bounds__(NT, 1) sample_cluster_kernel(SampleArgs a) {
       for (int i = tid; i < m; i += NT) {
         c.hs.cand_key[total + i] = o->hs.cand_key[i];
         c.hs.cand_w[total + i] = o->hs.cand_w[i];
-        c.ci[total + i] = o->ci[i];
+        c.hs.cand_i[total + i] = o->hs.cand_i[i];
       }
       total += m;
     }
   }
   cluster.sync();  // the other ranks' shared memory is no longer read
   if (rank != 0) return;
-  uint32_t floor_key = 0u;
-  if (use_k) floor_key = list_select<false>(c, total, 0u, 0.f, static_cast<uint32_t>(a.top_k), zmax);
-  if (use_p) {
-    float Z = c.st_Z;
-    if (use_k) {
-      float part = 0.f;
-      for (int i = tid; i < total; i += NT)
-        if (c.hs.cand_key[i] >= floor_key) part += expf(c.hs.cand_w[i] - zmax);
-      Z = block_sum(c.hs, part);
-    }
-    floor_key = list_select<true>(c, total, floor_key, a.top_p * Z, 0u, zmax);
-  }
-  bv = -INFINITY;
-  bi = 0x7fffffff;
-  for (int i = tid; i < total; i += NT) {
-    if (c.hs.cand_key[i] >= floor_key) {
-      const int idx = c.ci[i];
-      better(bv, bi, c.hs.cand_w[i] + gumbel(word(row_draw(a, row, static_cast<uint32_t>(idx >> 2)), idx & 3)), idx);
-    }
-  }
-  const int tok = block_argmax(c.hs, bv, bi);
-  if (tid == 0) {
-    a.out[row] = tok;
-    if (a.kept_min != nullptr) a.kept_min[row] = floor_key == 0u ? -INFINITY : kval(floor_key);
-  }
+  finish_list(c.hs, a, row, total, zmax, c.st_Z);
 }
 
 int g_attr_done[64];
