@@ -504,8 +504,9 @@ def run_sample(args, world: int, rank: int, local: int, dev, dist) -> None:
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
                      "algorithmic_bytes_per_step": alg, "avg_step_ms": avg_step_s * 1000.0,
-                     "note": "algorithmic bytes = one read of the logits; the radix selection reads them "
-                             "about 5 times"},
+                     "note": "algorithmic bytes = one read of the logits; with top-k or top-p the "
+                             "one-CTA path reads each row three times (max, window statistics, "
+                             "window collection)"},
         "e2e": {"value": world * B * args.steps / (e2e_ms / 1000.0), "unit": "rows/s",
                 "h2d_bytes_per_step": B * V * 4, "d2h_bytes_per_step": B * 4},
         "gpu_launches": args.steps,
