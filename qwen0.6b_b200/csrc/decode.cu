@@ -100,6 +100,7 @@ struct Workspace {
   uint64_t *inter;   // [IM]       fp16 payload (half(mlp_inter))
   uint64_t *part;    // [NKV][MAX_SPLITS][2][HD+2] fp32 payload (acc | m | l)
   uint64_t *amax;    // [2][MAX_CTAS] per-CTA argmax value / index
+  uint64_t *token;   // [1] the step's token, published by CTA 0
   uint32_t *kv_ready;
   unsigned long long *err;
 };
@@ -463,6 +464,10 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
 
   unsigned long long stall_ns = 0;
   const bool tracing = a.trace != nullptr;
+  auto prefetch = [&](const Piece &P) {
+    if (!((reinterpret_cast<uintptr_t>(P.src) & 15u) || (P.bytes & 15u) || P.bytes == 0))
+      bulk_prefetch_l2(P.src, P.bytes);
+  };
   auto issue = [&](const Piece &P) -> bool {
     const bool ok = issue_piece(sm, w, n, P.src, P.bytes, pol, tracing ? &stall_ns : nullptr);
     ++n;
@@ -508,6 +513,15 @@ __device__ __forceinline__ void producer(const DecodeArgs &a, Smem &sm) {
       for (int i = 0; i < 2 * gu_np && ok; ++i)
         ok = issue(seg_piece((i & 1) ? lp.w[9] : lp.w[8], 2 * H, gu_lo, gu_n, i >> 1, i & 1));
       for (int i = 0; i < d_np && ok; ++i) ok = issue(seg_piece(lp.w[10], 2 * IM, o_lo, o_n, i, 0));
+      // The next layer's q|k|v pieces get ring slots only when stage D
+      // releases its pieces, a few microseconds before stage A needs them:
+      // start pulling them into L2 now, so those copies are served from L2.
+      // (Prefetching the other stages' pieces too was slower: every prefetch
+      // is one more operation for the SM's copy engine.)
+      if (l + 1 < L) {
+        const LayerPtrs nx = load_layer(a.layers, l + 1);
+        for (int i = 0; i < qg.total; ++i) prefetch(qkv_piece(qg, nx, i));
+      }
       if (tr) tr[TR_P_END] = globaltimer_ns();
     }
     for (int i = 0; i < lm_np && ok; ++i) ok = issue(seg_piece(a.lm_head, 2 * H, lm_lo, lm_n, i, 0));
@@ -574,14 +588,39 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
   return v;
 }
 
+// s0 += lo(w) * lo(x) and s1 += hi(w) * hi(x) for two fp16 pairs packed in
+// 32-bit words, as sm_100's mixed-precision fma: the fp16 operands widen to
+// fp32 exactly, their product is exact in fp32 and each sum is rounded once,
+// which is fmaf on the widened values (the same bits), without separate
+// conversion instructions.
+__device__ __forceinline__ void fma_h2(float &s0, float &s1, uint32_t w, uint32_t x) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %2;\n\t"
+      "mov.b32 {xl, xh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, wl, xl, %0;\n\t"
+      "fma.rn.f32.f16 %1, wh, xh, %1;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "r"(w), "r"(x));
+}
+// s += lo(w) * lo(x), then s += hi(w) * hi(x) (one chain, same rounding).
+__device__ __forceinline__ void fma_h2_chain(float &s, uint32_t w, uint32_t x) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %1;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "fma.rn.f32.f16 %0, wl, xl, %0;\n\t"
+      "fma.rn.f32.f16 %0, wh, xh, %0;\n\t}"
+      : "+f"(s)
+      : "r"(w), "r"(x));
+}
+
 // Batch-1 GEMV of a stage with up to RMAX rows (QKV: <= 32, gate/up: <= 48
 // per CTA) on the CUDA cores: y[j] = W[j,:] . x for the `total` rows of the
 // row table (pieces n .. n+count-1, all landed before use).  Warp w takes
 // stage rows w, w + 8, ...; its lanes split K into 16-byte chunks (x's chunks
-// converted once and kept in registers), so each weight byte is read from
+// kept in registers), so each weight byte is read from
 // shared memory once, by consecutive lanes (no bank conflict, no row
-// padding).  fp16 products are exact in fp32; each lane keeps two fp32
-// chains, then a fixed-order warp sum: results are deterministic.
+// padding).  Products use the mixed-precision fma (fma_h2); each lane keeps two
+// fp32 chains, then a fixed-order warp sum: results are deterministic.
 // epi(kind, matrix_row, dot) runs on thread j for stage row j < total.
 template <int K, int RMAX, class Epi>
 __device__ __forceinline__ void gemv_wr(Smem &sm, uint32_t &n, int count, int total,
@@ -590,18 +629,9 @@ __device__ __forceinline__ void gemv_wr(Smem &sm, uint32_t &n, int count, int to
   constexpr int RPW = RMAX / NCW;      // rows per warp
   static_assert(K % 256 == 0 && RMAX % NCW == 0 && RMAX <= MAX_TILES * 16, "gemv_wr shape");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float xf[CH][8];
+  uint4 xw[CH];
 #pragma unroll
-  for (int i = 0; i < CH; ++i) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(x + 8 * (lane + 32 * i));
-    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __half22float2(h[j]);
-      xf[i][2 * j] = f.x;
-      xf[i][2 * j + 1] = f.y;
-    }
-  }
+  for (int i = 0; i < CH; ++i) xw[i] = *reinterpret_cast<const uint4 *>(x + 8 * (lane + 32 * i));
   float res[RPW];
 #pragma unroll
   for (int q = 0; q < RPW; ++q) {
@@ -613,13 +643,10 @@ __device__ __forceinline__ void gemv_wr(Smem &sm, uint32_t &n, int count, int to
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const __half2 *h = reinterpret_cast<const __half2 *>(&wv[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(h[j]);
-        s0 = fmaf(f.x, xf[i][2 * j], s0);
-        s1 = fmaf(f.y, xf[i][2 * j + 1], s1);
-      }
+      fma_h2(s0, s1, wv[i].x, xw[i].x);
+      fma_h2(s0, s1, wv[i].y, xw[i].y);
+      fma_h2(s0, s1, wv[i].z, xw[i].z);
+      fma_h2(s0, s1, wv[i].w, xw[i].w);
     }
     res[q] = s0 + s1;
   }
@@ -659,17 +686,9 @@ __device__ __forceinline__ void gemv_cc(Smem &sm, uint32_t &n, int count, int to
   constexpr int CH = K / 4 / NCT;  // chunks per thread
   static_assert(K % (4 * NCT) == 0, "K must split into 4-element chunks over the consumer threads");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float xf[CH][4];
+  uint2 xw[CH];
 #pragma unroll
-  for (int i = 0; i < CH; ++i) {
-    const uint2 u = *reinterpret_cast<const uint2 *>(x + 4 * (tid + NCT * i));
-    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
-    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
-    xf[i][0] = lo.x;
-    xf[i][1] = lo.y;
-    xf[i][2] = hi.x;
-    xf[i][3] = hi.y;
-  }
+  for (int i = 0; i < CH; ++i) xw[i] = *reinterpret_cast<const uint2 *>(x + 4 * (tid + NCT * i));
   // All loads first, with no branch between them (rows >= total are
   // padding entries that point at row 0: valid memory, results unused).
   uint2 wv[8][CH];
@@ -685,12 +704,8 @@ __device__ __forceinline__ void gemv_cc(Smem &sm, uint32_t &n, int count, int to
     float s = 0.f;
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&wv[r][i].x));
-      const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&wv[r][i].y));
-      s = fmaf(lo.x, xf[i][0], s);
-      s = fmaf(lo.y, xf[i][1], s);
-      s = fmaf(hi.x, xf[i][2], s);
-      s = fmaf(hi.y, xf[i][3], s);
+      fma_h2_chain(s, wv[r][i].x, xw[i].x);
+      fma_h2_chain(s, wv[r][i].y, xw[i].y);
     }
     acc[r] = s;
   }
@@ -1402,46 +1417,63 @@ __device__ __forceinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const Wai
 
 // ---------------------------------------------------------------- stage G
 // Global argmax over the per-CTA results (megakernel.cu:1114-1144), lowest
-// index among equal maxima.  Sets *token (uniform).
+// index among equal maxima.  CTA 0 gathers the per-CTA pairs and publishes
+// the token in one handoff word, which the other CTAs poll with one thread
+// each (every CTA gathering all pairs put ~150 pollers on the same few L2
+// lines).  Sets *token (uniform).
 __device__ __forceinline__ bool stage_g(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
                                         int s, int *token, unsigned long long *tr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int C = gridDim.x;
-  float v = -INFINITY;
-  int id = 0x7fffffff;
-  if (tid < C) {
-    uint32_t u[2];
-    const uint32_t eps_ = a.epoch_base + static_cast<uint32_t>(s);
-    st.fail |= !ll_gather<2>(w, [&](int i) { return a.ws.amax + i * MAX_CTAS + tid; }, eps_, u, W_G);
-    v = __uint_as_float(u[0]);
-    id = static_cast<int>(u[1]);
-  }
+  const uint32_t eps_ = a.epoch_base + static_cast<uint32_t>(s);
+  int bi = 0;
+  if (blockIdx.x == 0) {
+    float v = -INFINITY;
+    int id = 0x7fffffff;
+    if (tid < C) {
+      uint32_t u[2];
+      st.fail |= !ll_gather<2>(w, [&](int i) { return a.ws.amax + i * MAX_CTAS + tid; }, eps_, u, W_G);
+      v = __uint_as_float(u[0]);
+      id = static_cast<int>(u[1]);
+    }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, id, o);
-    if (ov > v || (ov == v && oi < id)) {
-      v = ov;
-      id = oi;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, id, o);
+      if (ov > v || (ov == v && oi < id)) {
+        v = ov;
+        id = oi;
+      }
     }
+    if (lane == 0) {
+      sm.gmax_val[warp] = v;
+      sm.gmax_idx[warp] = id;
+    }
+    if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+    float bv = sm.gmax_val[0];
+    bi = sm.gmax_idx[0];
+    for (int i = 1; i < NCW; ++i) {
+      const float vv = sm.gmax_val[i];
+      const int ii = sm.gmax_idx[i];
+      if (vv > bv || (vv == bv && ii < bi)) {
+        bv = vv;
+        bi = ii;
+      }
+    }
+    if (tid == 0) {
+      ll_store(a.ws.token, static_cast<uint32_t>(bi), eps_);
+      a.out_tokens[s] = bi;
+    }
+  } else {
+    if (tid == 0) {
+      uint32_t u[1];
+      st.fail |= !ll_gather<1>(w, [&](int) { return a.ws.token; }, eps_, u, W_G);
+      sm.gmax_idx[0] = static_cast<int>(u[0]);
+    }
+    if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
+    bi = sm.gmax_idx[0];
   }
-  if (lane == 0) {
-    sm.gmax_val[warp] = v;
-    sm.gmax_idx[warp] = id;
-  }
-  if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
   trace_mark(tr, 3);
-  float bv = sm.gmax_val[0];
-  int bi = sm.gmax_idx[0];
-  for (int i = 1; i < NCW; ++i) {
-    const float vv = sm.gmax_val[i];
-    const int ii = sm.gmax_idx[i];
-    if (vv > bv || (vv == bv && ii < bi)) {
-      bv = vv;
-      bi = ii;
-    }
-  }
-  if (blockIdx.x == 0 && tid == 0) a.out_tokens[s] = bi;
   *token = (bi >= 0 && bi < VOCAB) ? bi : 0;
   trace_mark(tr, 4);
   if (tr != nullptr && tid == 0) tr[6] = static_cast<unsigned long long>(clock64());
@@ -1547,7 +1579,7 @@ __global__ void selftest_wait_kernel(uint64_t *word, unsigned long long *err, lo
 }
 
 // Handoff words of one decode launch (the Workspace layout below), plus 32
-// words for the KV-ready counter and the status word.
+// words for the KV-ready counter, the status word and the published token.
 constexpr size_t WS_LL_WORDS = H + QKV_ROWS + QS / 2 + H + IM +
                                static_cast<size_t>(NKV) * MAX_SPLITS * 2 * (HD + 2) + 2 * MAX_CTAS;
 constexpr size_t WS_TAIL_WORDS = 32;
@@ -1646,6 +1678,7 @@ void bind_workspace(DevState &d, void *mem, int sms) {
   d.ws.amax = p; p += 2 * MAX_CTAS;
   d.ws.kv_ready = reinterpret_cast<uint32_t *>(p);
   d.ws.err = reinterpret_cast<unsigned long long *>(p) + 4;
+  d.ws.token = p + 8;
   d.mem = mem;
   d.ll_bytes = WS_LL_WORDS * sizeof(uint64_t);
   d.num_sms = sms;
@@ -1747,6 +1780,7 @@ int launch_on(DevState &d, DecodeArgs &a, cudaStream_t st) {
   const uint64_t need = static_cast<uint64_t>(a.num_steps) * (a.num_layers + 1) + 2;
   if (static_cast<uint64_t>(d.epoch) + need >= 0xfffffff0ull) {
     cudaMemsetAsync(d.mem, 0, d.ll_bytes, st);
+    cudaMemsetAsync(d.ws.token, 0, sizeof(uint64_t), st);
     d.epoch = 1;
   }
   a.epoch_base = d.epoch;
