@@ -80,6 +80,9 @@ constexpr int MAX_OWN = 64;           // rows per CTA of o_proj/down/gate-up
 constexpr int MAX_STAGE_ROWS = 48;    // GEMV rows per CTA and stage (C >= 128: QKV 32, gate+up 48)
 constexpr int MAX_TILES = MAX_STAGE_ROWS / 16;
 constexpr uint32_t BAR_ID = 1;
+// Layers whose norm-weight pointers the consumers keep in shared memory (read
+// once per launch instead of a dependent global load at every stage start).
+constexpr int NTAB_LAYERS = 32;
 
 enum Status : uint32_t {
   ST_OK = 0,
@@ -189,6 +192,7 @@ struct __align__(128) Smem {
   float cmb_f[2][MAX_SPLITS];                        // split rescale factor exp(m_j - M) per head
   uint32_t rowaddr[MAX_TILES * 16];  // smem address of each GEMV stage row (padding rows -> row 0)
   int rowinfo[MAX_TILES * 16];       // matrix row | kind << 24
+  const __half *ntab[NTAB_LAYERS][4];  // norm weights of the first layers: input, q, k, post
   float mred[NCW][MAX_TILES * 16];   // per-warp partial dot products
   unsigned long long trace_fullwait;
   float wmax_val[NCW];
@@ -783,6 +787,13 @@ __device__ __forceinline__ const __half *layer_ptr(const LDGLayerWeight *t, int 
       __ldg(reinterpret_cast<const unsigned long long *>(t + l) + idx));
 }
 
+// Norm weights k (0 input, 1 q, 2 k, 3 post-attention) of layer l: the table
+// entry packed at LDGLayerWeight slot 0 / 4 / 5 / 7.
+__device__ __forceinline__ int norm_slot(int k) { return k == 0 ? 0 : (k == 1 ? 4 : (k == 2 ? 5 : 7)); }
+__device__ __forceinline__ const __half *norm_ptr(const Smem &sm, const DecodeArgs &a, int l, int k) {
+  return l < NTAB_LAYERS ? sm.ntab[l][k] : layer_ptr(a.layers, l, norm_slot(k));
+}
+
 struct Rows {
   int lo, n;
 };
@@ -815,10 +826,13 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
   const QkvGeom qg = qkv_geom(C, c);
   const LayerPtrs lp{};  // consumers only need row ranges, not addresses
   const int total = prep_rows<H>(sm, st.n, qg.total, [&](int i) { return qkv_piece(qg, lp, i); });
-  const __half *nw = layer_ptr(a.layers, l, 0);
-  float wv[4], h[4];
+  // Norm weights: loaded now, converted only where they are used (after the
+  // hidden-vector gather), so their latency hides behind the gather.
+  const __half *nw = norm_ptr(sm, a, l, 0);
+  __half wr[4];
+  float h[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(nw + tid + NCT * i));
+  for (int i = 0; i < 4; ++i) wr[i] = __ldg(nw + tid + NCT * i);
   st.fail |= !wait_pieces(sm, w, st.n, qg.total, W_A);
   if (tr != nullptr) {
     __syncwarp();
@@ -846,7 +860,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
   trace_mark(tr, TR_A1);
   const float inv = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) sm.xa[tid + NCT * i] = __float2half(h[i] * (inv * wv[i]));
+  for (int i = 0; i < 4; ++i) sm.xa[tid + NCT * i] = __float2half(h[i] * (inv * __half2float(wr[i])));
   named_bar_sync(BAR_ID, NCT);
   gemv_wr<H, 32>(
       sm, st.n, qg.total, total, sm.xa,
@@ -872,18 +886,18 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
   trace_mark(tr, TR_B0);
   // Loads that do not depend on this layer's activations go first.
   const bool rope_warp = warp < 2 || (ag.last && warp == 2);
-  float nwv[4] = {0.f, 0.f, 0.f, 0.f}, csv[4] = {0.f, 0.f, 0.f, 0.f}, snv[4] = {0.f, 0.f, 0.f, 0.f};
+  __half nwv[4], csv[4], snv[4];  // converted where used, after the q|k|v gather
   if (rope_warp) {
-    const __half *nw = layer_ptr(a.layers, l, warp < 2 ? 4 : 5);
+    const __half *nw = norm_ptr(sm, a, l, warp < 2 ? 1 : 2);
     const __half *cosp = a.cos_t + static_cast<size_t>(p) * HD;
     const __half *sinp = a.sin_t + static_cast<size_t>(p) * HD;
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
       const int i = lane + 32 * it;
       const int ri = it < 2 ? i : i - HD / 2;
-      nwv[it] = __half2float(__ldg(nw + i));
-      csv[it] = __half2float(__ldg(cosp + ri));
-      snv[it] = __half2float(__ldg(sinp + ri));
+      nwv[it] = __ldg(nw + i);
+      csv[it] = __ldg(cosp + ri);
+      snv[it] = __ldg(sinp + ri);
     }
   }
   {
@@ -920,12 +934,13 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
     const float inv = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
     float vals[4];
 #pragma unroll
-    for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), nwv[it]);
+    for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), __half2float(nwv[it]));
 #pragma unroll
     for (int it = 0; it < 4; ++it) {
       const int i = lane + 32 * it;
-      const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], csv[it]), __fmul_rn(vals[it + 2], snv[it]))
-                             : __fadd_rn(__fmul_rn(vals[it - 2], snv[it]), __fmul_rn(vals[it], csv[it]));
+      const float c = __half2float(csv[it]), sn = __half2float(snv[it]);
+      const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], c), __fmul_rn(vals[it + 2], sn))
+                             : __fadd_rn(__fmul_rn(vals[it - 2], sn), __fmul_rn(vals[it], c));
       const __half hr = __float2half(r);
       if (warp < 2) sm.q_rot[warp][i] = hr;
       else sm.k_fresh[i] = hr;
@@ -1237,10 +1252,11 @@ __device__ __forceinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const Wai
   const int np = 2 * npieces(gu.n, 2 * H);
   const int total = prep_rows<H>(
       sm, st.n, np, [&](int i) { return seg_piece(nullptr, 2 * H, gu.lo, gu.n, i >> 1, i & 1); });
-  const __half *nw = layer_ptr(a.layers, l, 7);
-  float wv[4], h[4];
+  const __half *nw = norm_ptr(sm, a, l, 3);  // converted after the gather, as in stage A
+  __half wr[4];
+  float h[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(nw + tid + NCT * i));
+  for (int i = 0; i < 4; ++i) wr[i] = __ldg(nw + tid + NCT * i);
   st.fail |= !wait_pieces(sm, w, st.n, np, W_D);
   {
     uint32_t u[4];
@@ -1258,7 +1274,7 @@ __device__ __forceinline__ bool stage_d(Smem &sm, const DecodeArgs &a, const Wai
   const float rstd = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    sm.xa[tid + NCT * i] = __float2half(__half2float(__float2half(h[i])) * rstd * wv[i]);
+    sm.xa[tid + NCT * i] = __float2half(__half2float(__float2half(h[i])) * rstd * __half2float(wr[i]));
   named_bar_sync(BAR_ID, NCT);
   gemv_wr<H, 48>(sm, st.n, np, total, sm.xa, [&](int kind, int row, float dot) {
     (kind == 0 ? sm.g_out : sm.u_out)[row - gu.lo] = dot;
@@ -1503,6 +1519,9 @@ __device__ __forceinline__ void consumer(const DecodeArgs &a, Smem &sm) {
       token = 0;
     }
   }
+  for (int i = threadIdx.x; i < min(L, NTAB_LAYERS) * 4; i += NCT)
+    sm.ntab[i >> 2][i & 3] = layer_ptr(a.layers, i >> 2, norm_slot(i & 3));
+  named_bar_sync(BAR_ID, NCT);
   int s = 0;
   for (s = 0; s < a.num_steps; ++s) {
     const int p = a.start_pos + s;
