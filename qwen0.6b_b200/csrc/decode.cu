@@ -1088,8 +1088,22 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
         const uint2 *vcol = reinterpret_cast<const uint2 *>(sm.ring[pn % NSLOTS]) + dq;
         const float2 *pr = reinterpret_cast<const float2 *>(sm.sc[t0]);
         const int cnt = min(KV_TOK_PER_PIECE, n_old - t0);
+        if (cnt == KV_TOK_PER_PIECE) {
+          // Full piece: this thread's 6 tokens, all loads first.
+          constexpr int TPT = KV_TOK_PER_PIECE / 8;
+          uint2 vv[TPT];
+          float2 pp[TPT];
+#pragma unroll
+          for (int k = 0; k < TPT; ++k) {
+            vv[k] = vcol[(ts + 8 * k) * (HD / 4)];
+            pp[k] = pr[ts + 8 * k];
+          }
+#pragma unroll
+          for (int k = 0; k < TPT; ++k) pv_add(vv[k], pp[k]);
+        } else {
 #pragma unroll 2
-        for (int tt = ts; tt < cnt; tt += 8) pv_add(vcol[tt * (HD / 4)], pr[tt]);
+          for (int tt = ts; tt < cnt; tt += 8) pv_add(vcol[tt * (HD / 4)], pr[tt]);
+        }
       }
       if (fresh && ts == (n_old & 7))
         pv_add(reinterpret_cast<const uint2 *>(sm.qkv_raw + 3 * HD)[dq],
@@ -1334,9 +1348,10 @@ __device__ __forceinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const Wai
   trace_mark(tr, 0);
   if (tr != nullptr && tid == 0) tr[5] = static_cast<unsigned long long>(clock64());
   {
-    float wv[4], h[4];
+    __half wr[4];  // converted where used, after the gather
+    float h[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) wv[i] = __half2float(__ldg(a.final_norm + tid + NCT * i));
+    for (int i = 0; i < 4; ++i) wr[i] = __ldg(a.final_norm + tid + NCT * i);
     uint32_t u[4];
     st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.hidden + tid + NCT * i; }, ep_last, u, W_F);
     float ss = 0.f;
@@ -1352,7 +1367,7 @@ __device__ __forceinline__ bool stage_f(Smem &sm, const DecodeArgs &a, const Wai
     const float inv = rsqrtf(tot / static_cast<float>(H) + RMS_EPS);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float nv = h[i] * inv * wv[i];
+      const float nv = h[i] * inv * __half2float(wr[i]);
       sm.xf[tid + NCT * i] = nv;
       if (c == 0) a.norm_out[tid + NCT * i] = nv;
     }
