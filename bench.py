@@ -702,6 +702,7 @@ def main() -> None:
     dec = Decoder(weights=w_gpu, verbose=False)
 
     plen, gen = args.prompt_len, args.gen
+    cfg_name = {(16, 64): "config 1", (1920, 128): "config 2"}.get((plen, gen), "config 2 shape")
     g = torch.Generator().manual_seed(SEED + 1)
     prompt = torch.randint(0, 151936, (plen,), generator=g).tolist()
     first = None
@@ -779,7 +780,7 @@ def main() -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded random-init weights, uniform-random token ids)",
-        "config": {"workload": f"config 2: batch-1 {'sampled (temperature 0.8, top-k 50, top-p 0.9)' if args.sampled else 'greedy'}"
+        "config": {"workload": f"{cfg_name}: batch-1 {'sampled (temperature 0.8, top-k 50, top-p 0.9)' if args.sampled else 'greedy'}"
                                f" decode, {plen}-token seeded prompt "
                                f"prefilled (untimed), {gen} steps at positions {plen}..{plen + gen - 1}"
                                " per step",
