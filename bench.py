@@ -18,6 +18,13 @@ position 1920 (the KV cache of the prompt stays resident; positions
            HBM copy bandwidth.
 ``cpu_baseline`` the CPU oracle (a C restatement of the upstream algorithm)
            on this host's cores, on a bounded sample of the same workload.
+``cpu_baseline_hf`` the comparator upstream's own benchmark uses: HF
+           transformers Qwen3ForCausalLM in fp32 on the host cores (thread
+           count and torch.get_num_threads() recorded), a bounded sample.
+``batched`` the config-4 result (below) at the same number of GPUs, measured
+           after the decode workload in the same run, so that every default
+           run -- the 1/2/4/8-GPU scaling runs included -- carries the batched
+           tok/s; ``--no-batched`` skips it.
 
 Multi-GPU: single-sequence decode does not shard; ``--gpus N`` runs N
 independent replicas (one process per GPU) and reports their aggregate.
@@ -27,8 +34,9 @@ GPU, seeded prompt lengths uniform in [32, 512] and uniform token ids,
 prefilled with batched steps (untimed); one bench step = one batched greedy
 step of all 256 sequences (256 tokens).  Sequences are sharded per GPU (seeds
 offset by rank) with no collective; ``value`` is the aggregate tok/s.
-``--impl reference`` times the upstream algorithm's CPU restatement (the only
-CPU implementation of this path) with all host threads, rank 0 only.
+``--impl reference`` times the upstream algorithm's CPU restatement (the C
+oracle, kind "port") with all host threads, rank 0 only; each of its steps is a
+sample of 16 consecutive tokens of config 2's per-token work.
 """
 from __future__ import annotations
 
@@ -167,35 +175,97 @@ def cpu_baseline(weights_cpu: dict, seconds: float = 12.0, start: int = PROMPT_L
                       f"{start + n} over a seeded random {start}-position KV cache ({dt:.1f} s)"}
 
 
+REF_TOKENS_PER_STEP = 16
+
+
 def run_reference_arm(args, rank: int) -> None:
+    """The upstream algorithm's CPU restatement (the C oracle, all host
+    threads) on config 2's per-token work.  One reference "step" is a sample of
+    REF_TOKENS_PER_STEP consecutive greedy tokens at positions 1920.. over a
+    seeded 1920-position KV cache: the line's steps, ms_per_step and value
+    describe exactly those timed tokens (the GPU arm's step is 128 tokens)."""
     if rank != 0:
         return
     sys.path.insert(0, ROOT)
+    from oracle.oracle import OracleModel
     from qwen_weights import synthetic_weights
 
     w = synthetic_weights(seed=SEED)
-    per = max(3.0, 30.0 / max(1, args.steps + args.warmup))
-    for _ in range(args.warmup):
-        cpu_baseline(w, seconds=1.0)
-    vals = []
-    samples = []
-    for _ in range(args.steps):
-        cb = cpu_baseline(w, seconds=per)
-        vals.append(cb["value"])
-        samples.append(cb)
-    v = statistics.mean(vals)
-    cb = dict(samples[-1])
-    cb["value"] = v
+    threads = len(os.sched_getaffinity(0))
+    orc = OracleModel(w, nthreads=threads)
+    g = torch.Generator().manual_seed(1)
+    orc.k_cache[:, :, :PROMPT_LEN] = torch.randn(28, 8, PROMPT_LEN, 128, generator=g).half()
+    orc.v_cache[:, :, :PROMPT_LEN] = torch.randn(28, 8, PROMPT_LEN, 128, generator=g).half()
+
+    def sample(step: int) -> float:
+        # Positions wrap inside the 128-token range, so any K stays in bounds.
+        orc.position = PROMPT_LEN + (step * REF_TOKENS_PER_STEP) % (GEN - REF_TOKENS_PER_STEP + 1)
+        tok = 1
+        t0 = time.perf_counter()
+        for _ in range(REF_TOKENS_PER_STEP):
+            tok = orc.step(tok)["token"]
+        return time.perf_counter() - t0
+
+    for i in range(args.warmup):
+        sample(i)
+    secs = [sample(args.warmup + i) for i in range(args.steps)]
+    total = sum(secs)
+    v = REF_TOKENS_PER_STEP * args.steps / total
+    desc = (f"{args.steps} samples of {REF_TOKENS_PER_STEP} consecutive greedy tokens of the 28-layer "
+            f"C oracle at positions {PROMPT_LEN}..{PROMPT_LEN + GEN - 1} over a seeded random "
+            f"{PROMPT_LEN}-position KV cache, {threads} threads ({total:.1f} s timed)")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * GEN / v, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": 1000.0 * total / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": "config 2 per-token work: batch-1 greedy decode at positions "
-                                   "1920..2047, CPU oracle sample", "batch": 1,
-                       "prompt_len": PROMPT_LEN, "gen_steps": GEN, "parallelism": "cpu"},
-            "cpu_baseline": cb,
+                                   f"1920..2047; one step = a sample of {REF_TOKENS_PER_STEP} tokens "
+                                   "(the GPU arm's step is 128 tokens)",
+                       "batch": 1, "prompt_len": PROMPT_LEN, "gen_steps": GEN,
+                       "tokens_per_step": REF_TOKENS_PER_STEP, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": desc},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def hf_cpu_baseline(weights_cpu: dict, start: int = PROMPT_LEN, seconds: float = 10.0) -> dict:
+    """The comparator upstream's own benchmark uses (Model/benchmark.py:48-84):
+    HF transformers Qwen3ForCausalLM in fp32 on the host cores, greedy decode
+    with the KV cache after an untimed prefill of a seeded `start`-token
+    prompt; a bounded sample of decode steps is timed."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from qwen_weights import hf_state_dict
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
+                      head_dim=128, rope_theta=1e6, rms_norm_eps=1e-6, tie_word_embeddings=True,
+                      max_position_embeddings=2048, attention_bias=False)
+    with torch.device("meta"):
+        m = Qwen3ForCausalLM(cfg)
+    m.load_state_dict(hf_state_dict(weights_cpu), strict=False, assign=True)
+    m.tie_weights()
+    m = m.float().eval()
+    g = torch.Generator().manual_seed(SEED + 1)
+    ids = torch.randint(0, 151936, (1, start), generator=g)
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        out = m(ids, use_cache=True)
+        prefill_s = time.perf_counter() - t0
+        past, tok = out.past_key_values, out.logits[:, -1:].argmax(-1)
+        n, t0 = 0, time.perf_counter()
+        while (time.perf_counter() - t0 < seconds or n < 3) and start + n < 2048:
+            out = m(tok, past_key_values=past, use_cache=True)
+            past, tok = out.past_key_values, out.logits[:, -1:].argmax(-1)
+            n += 1
+        dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "torch_threads": torch.get_num_threads(),
+            "kind": "hf-fp32",
+            "sample": f"{n} greedy decode steps of HF Qwen3ForCausalLM fp32 (transformers "
+                      f"{__import__('transformers').__version__}) at positions {start}..{start + n - 1} "
+                      f"after a {start}-token prefill ({prefill_s:.1f} s, untimed), {dt:.1f} s timed"}
 
 
 def batched_cpu_baseline(weights_cpu: dict, pos: int, seconds: float = 10.0) -> dict:
@@ -203,11 +273,23 @@ def batched_cpu_baseline(weights_cpu: dict, pos: int, seconds: float = 10.0) -> 
     oracle decodes one sequence at a time; its tok/s is the CPU rate for this
     per-token work), a bounded sample."""
     cb = cpu_baseline(weights_cpu, seconds=seconds, start=pos)
-    cb["sample"] = "one sequence, " + cb["sample"] + f" (batched workload mean position {pos})"
+    cb["sample"] = ("one sequence, " + cb["sample"] + f" (batched workload mean position {pos}); "
+                    "extrapolated to the batch: the CPU decodes the sequences one after another, "
+                    "so its tok/s for the batch is this one sequence's rate")
+    cb["extrapolated"] = True
     return cb
 
 
 def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
+    line = batched_line(args, world, rank, local, dev, dist)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def batched_line(args, world: int, rank: int, local: int, dev, dist, with_cpu: bool = True) -> dict:
     """Config 4: batched greedy decode of independent sequences per GPU."""
     from batched import BatchedDecoder
     from qwen_weights import synthetic_weights
@@ -333,15 +415,11 @@ def run_batched(args, world: int, rank: int, local: int, dev, dist) -> None:
         "gpu_launches": args.steps * (args.layers * 11 + 3),
         "clocks": clk,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and with_cpu:
         mean_pos = int(statistics.mean(int(p.float().mean()) for p in pos_list))
         line["cpu_baseline"] = batched_cpu_baseline(w_cpu, mean_pos)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     bd.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
 
 
 def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
@@ -643,6 +721,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-hf-baseline", action="store_true",
+                    help="skip the HF transformers fp32 CPU figure of the default line")
+    ap.add_argument("--no-batched", action="store_true",
+                    help="default workload: skip the config-4 (batched) sub-record")
     ap.add_argument("--prompt-len", type=int, default=PROMPT_LEN,
                     help="prefilled tokens before the timed steps (workload: 1920)")
     ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (workload: 128)")
@@ -800,6 +882,17 @@ def main() -> None:
         line["roofline"]["note"] = "per token: one decode launch (logits written) + one sampling launch"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w_cpu)
+        if not args.no_hf_baseline:
+            line["cpu_baseline_hf"] = hf_cpu_baseline(w_cpu)
+    if not args.no_batched and (plen, gen) == (PROMPT_LEN, GEN) and not args.sampled:
+        # Config 4 at the same N (BASELINE's "batched tok/s at 1/2/4/8"), so
+        # every default run -- the driver's scaling runs included -- records it.
+        del dec, w_gpu
+        torch.cuda.empty_cache()
+        b = batched_line(args, world, rank, local, dev, dist, with_cpu=True)
+        keep = ("value", "unit", "ms_per_step", "steps", "warmup", "scaling", "config", "roofline",
+                "e2e", "gpu_launches", "clocks", "cpu_baseline")
+        line["batched"] = {k: b[k] for k in keep if k in b}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

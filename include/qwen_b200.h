@@ -97,8 +97,10 @@ void launch_ldg_generate_nosync(
  * synchronisation is not acceptable.
  * - The first call on each device does a one-time set-up with that device
  *   current: it looks the array up (cudaGetSymbolAddress, which may load this
- *   library's kernels on the device) and clears it with a synchronous memset.
- *   Make that first call before any stream capture.
+ *   library's kernels on the device), clears it (cudaMemset) and waits for the
+ *   device (cudaDeviceSynchronize), so that the clear cannot land during the
+ *   first launch on a non-blocking stream.  Make that first call before any
+ *   stream capture.
  * - The array is sized for at most 256 SMs and 32 attention splits per KV
  *   head; it does not grow with sequence length, steps or layers.  A device
  *   that would need more is rejected with an error; so are the arguments
@@ -106,8 +108,8 @@ void launch_ldg_generate_nosync(
  * - Calls on one device share the array: calls that overlap in time (other
  *   streams, other host threads without ordering) race and corrupt each other.
  *   Order them, e.g. on one stream.
- * - Device-side failures show as -1 tokens in output_log;
- *   qwen_b200_device_status() reports on the allocating launchers only.
+ * - Device-side failures show as -1 tokens in output_log, and
+ *   qwen_b200_device_status() reports their code and detail word.
  * Returns 0 when the launch was issued, else the qwen_b200_last_error() code.
  */
 int launch_ldg_generate_nosync_static_ws(
@@ -145,10 +147,16 @@ int qwen_b200_decode_step_dev(
  * qwen_b200_last_error: 0 if the calling thread's last launcher call was
  * accepted, else a nonzero code; a message is copied into msg (may be NULL).
  * qwen_b200_device_status: synchronises the device's work submitted so far,
- * then returns the device-side status word of the last decode launch on
- * `device` (0 = ok; else (code, where) packed as described in the source). */
+ * then returns the device-side status of the last decode launch on `device`
+ * of each workspace (the allocating launchers' and the static one of
+ * launch_ldg_generate_nosync_static_ws): 0 = ok, else the first failure's
+ * code, with its word ((code, where, CTA) packed as described in the source)
+ * in *detail.
+ * qwen_b200_workspace_info: whether each of the two per-device workspaces has
+ * been set up on `device` (1) or not (0); host-side only, no device call. */
 int qwen_b200_last_error(char *msg, int msg_len);
 int qwen_b200_device_status(int device, uint64_t *detail);
+int qwen_b200_workspace_info(int device, int *alloc_ready, int *static_ready);
 
 /* Wall-clock limit for every bounded wait inside the decode kernel,
  * nanoseconds (default 2e9).  Applies to later launches on all devices. */

@@ -84,9 +84,22 @@ def build(ref: str) -> bool:
     return True
 
 
+def reference_dir() -> str:
+    """$QWEN_REFERENCE_DIR, else BASELINE.json's "reference_path" (repo root)."""
+    env = os.environ.get("QWEN_REFERENCE_DIR")
+    if env:
+        return env
+    try:
+        import json
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path") or ""
+    except (OSError, ValueError):
+        return ""
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("QWEN_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--ref", default=reference_dir())
     args = ap.parse_args()
     build(args.ref)
     sys.exit(0)

@@ -1739,17 +1739,28 @@ DevState *get_dev(int *dev_out) {
     fail_msg(5, "cudaMalloc(%zu) for the decode workspace: %s", total, cudaGetErrorString(e));
     return nullptr;
   }
-  cudaMemset(mem, 0, total);
+  // The clear runs on the legacy default stream, which is not ordered with
+  // the non-blocking streams callers launch on: wait for it here, so the
+  // first launch cannot see it land mid-run.
+  e = cudaMemset(mem, 0, total);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(mem);
+    fail_msg(5, "clearing the decode workspace on device %d: %s", *dev_out, cudaGetErrorString(e));
+    return nullptr;
+  }
   bind_workspace(d, mem, sms);
   return &d;
 }
 
 // Workspace of launch_ldg_generate_nosync_static_ws: the module's static
 // array, looked up once per device (with that device current).  The lookup
-// may load the module on that device and the clearing is a synchronous
-// memset, which is why this set-up belongs before any stream capture.
-// Cleared here because every handoff word must start with an epoch no launch
-// uses (0), and the status word and KV-ready counter at 0.
+// may load the module on that device, and the clearing is followed by a
+// cudaDeviceSynchronize (the clear runs on the legacy default stream, which
+// is not ordered with the caller's non-blocking streams), which is why this
+// set-up belongs before any stream capture.  Cleared here because every
+// handoff word must start with an epoch no launch uses (0), and the status
+// word and KV-ready counter at 0.
 DevState g_dev_static[64];
 
 DevState *get_dev_static(int *dev_out) {
@@ -1766,6 +1777,7 @@ DevState *get_dev_static(int *dev_out) {
     return nullptr;
   }
   e = cudaMemset(mem, 0, (WS_LL_WORDS + WS_TAIL_WORDS) * sizeof(uint64_t));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     fail_msg(6, "clearing the static decode workspace on device %d: %s", *dev_out,
              cudaGetErrorString(e));
@@ -1936,17 +1948,36 @@ int qwen_b200_device_status(int device, uint64_t *detail) {
   uint64_t word = 0;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    DevState &d = g_dev[device];
-    if (d.ready) {
-      cudaDeviceSynchronize();
-      if (cudaMemcpy(&word, d.ws.err, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess) rc = -2;
-      else if (static_cast<uint32_t>(word >> 32) == d.last_tag && (word & 0xffffffffull))
-        rc = static_cast<int>((word >> 24) & 0xff);
+    // The allocating launchers' workspace first, then the static one of
+    // launch_ldg_generate_nosync_static_ws: the first failure found is
+    // reported (each word only counts for its workspace's last launch).
+    bool synced = false;
+    for (DevState *d : {&g_dev[device], &g_dev_static[device]}) {
+      if (!d->ready || rc != 0) continue;
+      if (!synced) {
+        cudaDeviceSynchronize();
+        synced = true;
+      }
+      uint64_t w = 0;
+      if (cudaMemcpy(&w, d->ws.err, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        rc = -2;
+      } else if (static_cast<uint32_t>(w >> 32) == d->last_tag && (w & 0xffffffffull)) {
+        rc = static_cast<int>((w >> 24) & 0xff);
+        word = w;
+      }
     }
   }
   if (detail) *detail = word;
   cudaSetDevice(prev);
   return rc;
+}
+
+int qwen_b200_workspace_info(int device, int *alloc_ready, int *static_ready) {
+  if (device < 0 || device >= 64) return -1;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (alloc_ready) *alloc_ready = g_dev[device].ready ? 1 : 0;
+  if (static_ready) *static_ready = g_dev_static[device].ready ? 1 : 0;
+  return 0;
 }
 
 void launch_ldg_decode_direct(int input_token_id, int *output_token_id, const void *embed_weight,

@@ -27,6 +27,12 @@ DECODE_CASES = [
 # tokens are decoded at positions start, start+1, ...
 LONGCTX_CASES = [
     dict(name="s7_l2_p1920", seed=7, num_layers=2, start=1920, tokens=_tokens(11, 4), kv_seed=2024),
+    # The benchmarked long-context shape at full depth: the first positions of
+    # the timed range and its last positions (up to max_seq - 1 = 2047).
+    dict(name="s1234_l28_p1920", seed=1234, num_layers=28, start=1920, tokens=_tokens(12, 6),
+         kv_seed=2025),
+    dict(name="s1234_l28_p2042", seed=1234, num_layers=28, start=2042, tokens=_tokens(13, 6),
+         kv_seed=2026),
 ]
 
 OPS_CASE = dict(eps=1e-6, batches=[1, 8, 64, 256], swiglu_batches=[1, 8], seed=31337)

@@ -123,18 +123,25 @@ def record_steps(dec, toks, pos0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", choices=["decode", "ops"], default=None)
+    ap.add_argument("--only", choices=["decode", "longctx", "ops"], default=None)
+    ap.add_argument("--cases", default=None,
+                    help="comma-separated case names to (re)generate; default: all of the selected kind")
     args = ap.parse_args()
     os.makedirs(args.out, exist_ok=True)
-    if args.only != "ops":
+    if args.only in (None, "decode", "longctx"):
         run_decode(args)
-    if args.only != "decode":
+    if args.only in (None, "ops"):
         run_ops(args)
+
+
+def _selected(args, cases):
+    want = None if args.cases is None else set(args.cases.split(","))
+    return [c for c in cases if want is None or c["name"] in want]
 
 
 def run_decode(args):
     mk = _load_ref("qwen_megakernel_C")
-    for case in DECODE_CASES:
+    for case in (_selected(args, DECODE_CASES) if args.only != "longctx" else []):
         t0 = time.time()
         dec = RefDecoder(mk, case["seed"], case["num_layers"])
         rec = record_steps(dec, case["prompt"], 0)
@@ -147,7 +154,7 @@ def run_decode(args):
         print(f"decode {case['name']}: {time.time() - t0:.1f}s tokens={rec['out'].tolist()} gen={gen.tolist()}")
         del dec
         torch.cuda.empty_cache()
-    for case in LONGCTX_CASES:
+    for case in (_selected(args, LONGCTX_CASES) if args.only != "decode" else []):
         t0 = time.time()
         dec = RefDecoder(mk, case["seed"], case["num_layers"])
         kc, vc = longctx_cache(case)

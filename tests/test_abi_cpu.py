@@ -37,6 +37,16 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_workspace_info_before_any_launch():
+    """No launcher ran in this process: neither per-device workspace exists
+    (host-side query, no CUDA call)."""
+    lib = ctypes.CDLL(LIB)
+    a, b = ctypes.c_int(-1), ctypes.c_int(-1)
+    assert lib.qwen_b200_workspace_info(0, ctypes.byref(a), ctypes.byref(b)) == 0
+    assert (a.value, b.value) == (0, 0)
+    assert lib.qwen_b200_workspace_info(64, None, None) == -1
+
+
 def test_abi_version():
     lib = ctypes.CDLL(LIB)
     assert lib.qwen_b200_abi_version() == 2

@@ -118,17 +118,29 @@ def test_oracle_matches_upstream_decode(case, weights_2l, weights_28l):
 
 
 @pytest.mark.parametrize("case", LONGCTX_CASES, ids=[c["name"] for c in LONGCTX_CASES])
-def test_oracle_matches_upstream_long_context(case, weights_2l):
+def test_oracle_matches_upstream_long_context(case, weights_2l, weights_28l):
     g = _golden(f"ref_longctx_{case['name']}.npz")
-    orc = O.OracleModel(weights_2l, num_layers=case["num_layers"])
+    w = weights_28l if case["num_layers"] == 28 else weights_2l
+    assert case["seed"] == (1234 if case["num_layers"] == 28 else 7)
+    orc = O.OracleModel(w, num_layers=case["num_layers"])
     kc, vc = longctx_cache(case)
     orc.k_cache.copy_(kc)
     orc.v_cache.copy_(vc)
     orc.position = case["start"]
-    emb = weights_2l["embed_weight"]
+    emb = w["embed_weight"]
     for i, t in enumerate(g["inp"]):
+        pos = case["start"] + i
         r = orc.step(int(t))
-        _check(_logits(g["norm"][i], emb), _logits(r["norm_out"], emb), r["token"], f"longctx {i}")
+        ref_l = _logits(g["norm"][i], emb)
+        _check(ref_l, _logits(r["norm_out"], emb), r["token"], f"longctx {case['name']} step {i}")
+        top2 = torch.topk(ref_l, 2).values
+        if float(top2[0] - top2[1]) > MARGIN:
+            assert r["token"] == int(g["out"][i]), f"longctx {case['name']} step {i}"
+        for tag, li in (("first", 0), ("last", case["num_layers"] - 1)):
+            for kind, cache in (("k", orc.k_cache), ("v", orc.v_cache)):
+                ref_kv = torch.from_numpy(g[f"{kind}_{tag}"][i].view(np.float16).astype(np.float32))
+                d = float((ref_kv - cache[li, :, pos].float()).abs().max())
+                assert d < 5e-2, f"{kind} cache layer {li} step {i}: {d}"
 
 
 def test_oracle_matches_upstream_ops():
