@@ -243,10 +243,14 @@ def hf_cpu_baseline(weights_cpu: dict, start: int = PROMPT_LEN, seconds: float =
                       num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8,
                       head_dim=128, rope_theta=1e6, rms_norm_eps=1e-6, tie_word_embeddings=True,
                       max_position_embeddings=2048, attention_bias=False)
+    # Built on the meta device (no random init of 0.6 B parameters), then
+    # materialised and filled from the seeded weights; the rotary table is a
+    # non-persistent buffer, so it is rebuilt rather than loaded.
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
     with torch.device("meta"):
         m = Qwen3ForCausalLM(cfg)
     m.load_state_dict(hf_state_dict(weights_cpu), strict=False, assign=True)
-    m.tie_weights()
+    m.model.rotary_emb = Qwen3RotaryEmbedding(config=cfg)
     m = m.float().eval()
     g = torch.Generator().manual_seed(SEED + 1)
     ids = torch.randint(0, 151936, (1, start), generator=g)
@@ -436,9 +440,10 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
     sets = [(wg.clone(), wu.clone(), wd.clone()) for _ in range(8)]
     eps = OPS_CASE["eps"]
     stream = torch.cuda.current_stream(dev)
+    exact = True if args.exact else None  # None: tensor cores from 64 rows on
     for i in range(args.warmup):
-        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8])
-    ref = swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[0])[0].clone()
+        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8], exact=exact)
+    ref = swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[0], exact=exact)[0].clone()
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
@@ -451,7 +456,7 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
     t_start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
-        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8])
+        swiglu_fused.rmsnorm_forward_down(x, w, eps, *sets[i % 8], exact=exact)
         ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
@@ -467,7 +472,7 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
     t0 = time.perf_counter()
     for i in range(args.steps):
         d_x.copy_(h_x, non_blocking=True)
-        h_y.copy_(swiglu_fused.rmsnorm_forward_down(d_x, w, eps, *sets[0])[0], non_blocking=True)
+        h_y.copy_(swiglu_fused.rmsnorm_forward_down(d_x, w, eps, *sets[0], exact=exact)[0], non_blocking=True)
         stream.synchronize()
     e2e_ms = 1000.0 * (time.perf_counter() - t0)
     assert torch.equal(h_y, ref.cpu()), "non-deterministic operator output"
@@ -478,6 +483,7 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
     value = world * B * args.steps / (total_ms / 1000.0)
     e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
     alg = 3 * 1024 * 3072 * 2 + 1024 * 2 + 4 * B * 1024
+    tc = not args.exact and B >= 64
     avg_step_s = statistics.mean(step_ms) / 1000.0
     peaks = measured_peaks()
     achieved = alg / avg_step_s / 1e9
@@ -487,18 +493,23 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (x ~ N(0,1), norm weight ~ N(1,0.1), W ~ N(0,0.02))",
         "config": {"workload": f"config 3: RMSNorm + SwiGLU + down projection on [{B}, 1024], "
-                               "upstream fp16 accumulation order reproduced (bit-exact)",
+                               + ("tcgen05 GEMMs with fp32 accumulation" if tc else
+                                  "upstream fp16 accumulation order reproduced (bit-exact)"),
                    "batch": B, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "8 weight sets of 18.9 MB rotate (151 MB > L2)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
                      "algorithmic_bytes_per_step": alg, "avg_step_ms": avg_step_s * 1000.0,
-                     "note": "the serial fp16 chains (1024 + 3072 dependent adds) bound small batches"},
+                     "note": ("two tcgen05 GEMMs (gate|up with the SwiGLU epilogue, down with K split "
+                              "over a cluster) after the RMSNorm kernel" if tc else
+                              "the serial fp16 chains (1024 + 3072 dependent adds) bound small batches")},
         "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": B * 2048,
                 "d2h_bytes_per_step": B * 2048},
         "gpu_launches": args.steps * 3,
         "clocks": clk,
     }
+    if tc:
+        line["tflops"] = 2 * 3 * 1024 * 3072 * B / avg_step_s / 1e12
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
         threads = len(os.sched_getaffinity(0))
@@ -740,6 +751,8 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
+    ap.add_argument("--exact", action="store_true",
+                    help="ops workload: upstream's fp16 accumulation chains (bit-exact) at every batch size")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -39,6 +39,12 @@ extern "C" {
  */
 int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, const void *res,
                        void *workspace, int M, int N, int K, int ldo, int k_splits, void *stream);
+/* The same with the tile width chosen by the caller: bn = 64, 128 or 256
+ * output columns per CTA (0: by output size, as qwen_b200_gemm_f16); the
+ * argmax epilogue takes the default only.  No upstream counterpart. */
+int qwen_b200_gemm_f16_tiled(int epilogue, const void *a, const void *b, void *out, const void *res,
+                             void *workspace, int M, int N, int K, int ldo, int k_splits, int bn,
+                             void *stream);
 long long qwen_b200_gemm_argmax_workspace(int M, int N);
 
 /*

@@ -51,8 +51,9 @@ int qwen_b200_swiglu_forward(const void *x, const void *w_gate, const void *w_up
                              const void *b_gate, const void *b_up, void *out, void *gate_cache,
                              void *up_cache, long long rows, int hidden, int inter, void *stream);
 
-/* Bytes of device workspace qwen_b200_swiglu_forward_down needs (the SwiGLU
- * activations, rows x inter fp16, rounded up to 256). */
+/* Bytes of device workspace qwen_b200_swiglu_forward_down(_ex) needs: the
+ * SwiGLU activations, rows x inter fp16 (the fp16 chains) or their hi and lo
+ * fp16 parts (the tensor-core path), so 4 bytes per element, rounded up to 256. */
 long long qwen_b200_swiglu_forward_down_workspace(long long rows, int inter);
 
 /* out[r, h] = b_down[h] + sum_i s[r,i] w_down[i,h] in fp16 steps, where s is
@@ -64,7 +65,8 @@ int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void 
                                   const void *b_down, void *out, void *workspace,
                                   long long rows, int hidden, int inter, void *stream);
 
-/* Bytes of device workspace qwen_b200_rmsnorm_swiglu_down needs. */
+/* Bytes of device workspace qwen_b200_rmsnorm_swiglu_down(_ex) needs (the
+ * normed rows when `normed` is NULL, then the activations as above). */
 long long qwen_b200_rmsnorm_swiglu_down_workspace(long long rows, int hidden, int inter);
 
 /* The config-3 chain in one call: normed = rmsnorm(x, norm_weight, eps,
@@ -78,6 +80,30 @@ int qwen_b200_rmsnorm_swiglu_down(const void *x, const void *norm_weight, void *
                                   const void *b_down, void *normed, float *rms, void *out,
                                   void *workspace, long long rows, int hidden, int inter,
                                   void *stream);
+
+/* Dispatching forms of qwen_b200_swiglu_forward_down and
+ * qwen_b200_rmsnorm_swiglu_down (same arguments and workspace, plus `mode`);
+ * no upstream counterpart as entry points (upstream has only the fp16-chain
+ * kernels, swiglu.cu:267-310, :413-464).
+ *   mode 1   the fp16 chains above (bit-identical to upstream);
+ *   mode 0   tensor cores: gate and up as one tcgen05 GEMM with fp32
+ *            accumulation on the [hidden, inter] weights, s = half(g / (1 +
+ *            exp(-g)) * u) with g, u in fp32 (biases added in fp32), then the
+ *            down projection as a tcgen05 GEMM (fp32 accumulation, K split
+ *            inside a thread-block cluster), out = half(acc + b_down).  Needs
+ *            hidden and inter multiples of 64.  Closer to an fp32 evaluation
+ *            than upstream's fp16 accumulation, not bit-identical to it;
+ *   mode -1  tensor cores for rows >= 64 when the shape allows, else the chains. */
+int qwen_b200_swiglu_forward_down_ex(const void *x, const void *w_gate, const void *w_up,
+                                     const void *w_down, const void *b_gate, const void *b_up,
+                                     const void *b_down, void *out, void *workspace,
+                                     long long rows, int hidden, int inter, int mode, void *stream);
+int qwen_b200_rmsnorm_swiglu_down_ex(const void *x, const void *norm_weight, void *residual,
+                                     float eps, const void *w_gate, const void *w_up,
+                                     const void *w_down, const void *b_gate, const void *b_up,
+                                     const void *b_down, void *normed, float *rms, void *out,
+                                     void *workspace, long long rows, int hidden, int inter, int mode,
+                                     void *stream);
 
 /* Synchronises the current device, then returns 0 if no operator kernel has
  * given up a bounded wait since the last call, else the code it recorded

@@ -34,6 +34,8 @@
 #include <stdio.h>
 
 #include <new>
+#include <stdlib.h>
+#include <string.h>
 
 #include "gemm_tc_host.h"
 #include "host_err.h"
@@ -580,6 +582,10 @@ struct Plan {
   Workspace ws;
   KvGeom kg;
   GemmPlan g_qkv[64], g_o[64], g_gu[64], g_down[64], g_lm;
+  // Per projection (0 q|k|v, 1 o_proj, 2 gate/up, 3 down): K slices and how
+  // they are added (1: inside a thread-block cluster; 0: partial tiles in the
+  // workspace plus a reduction kernel).
+  int ksplit[4], kcluster[4];
   CUtensorMap tm_k;   // K pool as [pages * layers * 8 * page_tokens rows, 128], 64 x CH boxes, 128B swizzle
 };
 
@@ -648,13 +654,52 @@ int create_plan(void **handle, const QwenBatchedLayer *layers, int num_layers, c
   p->kg.num_pages = page_table != nullptr ? num_pages : num_seqs;
   p->kg.page_tokens = page_table != nullptr ? CH : max_seq;
   carve(static_cast<uint8_t *>(workspace), max_rows, p->max_splits, p->lm_tiles, &p->ws);
+  // Tiling of the four projections: tile width (0: by output size), K slices,
+  // cluster reduction.  QB200_GEMM_CFG="name:bn:ksplit:cluster,..." (names
+  // qkv, o, gu, down) overrides it, for tuning runs.
+  static const char *names[4] = {"qkv", "o", "gu", "down"};
+  int bn_cfg[4] = {0, 0, 0, 0};
+  const int ncols[4] = {QKV, H, 2 * IM, H};
+  const int kdims[4] = {H, QS, H, IM};
+  for (int i = 0; i < 4; ++i) {
+    p->ksplit[i] = ncols[i] == H ? KSPLIT : 1;
+    p->kcluster[i] = 0;
+  }
+  if (const char *env = getenv("QB200_GEMM_CFG")) {
+    char buf[256];
+    strncpy(buf, env, sizeof(buf) - 1);
+    buf[sizeof(buf) - 1] = 0;
+    for (char *tok = strtok(buf, ","); tok != nullptr; tok = strtok(nullptr, ",")) {
+      char name[16] = {0};
+      int bn = 0, ks = 1, cl = 0;
+      if (sscanf(tok, "%15[^:]:%d:%d:%d", name, &bn, &ks, &cl) < 2) continue;
+      for (int i = 0; i < 4; ++i) {
+        if (strcmp(name, names[i]) != 0) continue;
+        bn_cfg[i] = bn;
+        p->ksplit[i] = ks < 1 ? 1 : ks;
+        p->kcluster[i] = cl;
+      }
+    }
+  }
   int rc = 0;
+  for (int i = 0; i < 4 && rc == 0; ++i) {
+    // K slices: whole k-blocks each; partial tiles must fit the workspace,
+    // else the slices are added inside a cluster (at most 8).
+    if (p->ksplit[i] > kdims[i] / qb200tc::BK) p->ksplit[i] = kdims[i] / qb200tc::BK;
+    if (p->ksplit[i] > 1 && !p->kcluster[i] &&
+        static_cast<long long>(p->ksplit[i]) * ncols[i] > static_cast<long long>(KSPLIT) * H)
+      p->kcluster[i] = 1;
+    if (p->kcluster[i] && p->ksplit[i] > 8) p->ksplit[i] = 8;
+  }
   for (int l = 0; l < num_layers && rc == 0; ++l) {
     const QwenBatchedLayer &L = layers[l];
     rc = qb200_gemm_make_maps(&p->g_qkv[l], p->ws.xn, L.w_qkv, max_rows, QKV, H, H, H);
     if (!rc) rc = qb200_gemm_make_maps(&p->g_o[l], p->ws.attn, L.w_o, max_rows, H, QS, QS, QS);
     if (!rc) rc = qb200_gemm_make_maps(&p->g_gu[l], p->ws.sact, L.w_gu, max_rows, 2 * IM, H, H, H);
     if (!rc) rc = qb200_gemm_make_maps(&p->g_down[l], p->ws.inter, L.w_down, max_rows, H, IM, IM, IM);
+    GemmPlan *gp[4] = {&p->g_qkv[l], &p->g_o[l], &p->g_gu[l], &p->g_down[l]};
+    for (int i = 0; i < 4 && rc == 0; ++i)
+      if (bn_cfg[i] != 0) rc = qb200_gemm_set_bn(gp[i], bn_cfg[i]);
   }
   if (!rc) rc = qb200_gemm_make_maps(&p->g_lm, p->ws.norm16, embed, max_rows, VOCAB, H, H, H);
   const long long k_rows = static_cast<long long>(p->kg.num_pages) * num_layers * NKV * p->kg.page_tokens;
@@ -706,6 +751,14 @@ int qwen_b200_batched_create_paged(void **handle, const QwenBatchedLayer *layers
 
 namespace {
 
+// One projection GEMM of a layer with its plan's K split.
+int run_proj(Plan *p, int i, const GemmPlan &gp, int epi, const GemmArgs &g, float *partial,
+             cudaStream_t st) {
+  if (p->ksplit[i] > 1)
+    return qb200_gemm_run_splitk(gp, epi, g, p->ksplit[i], p->kcluster[i] ? nullptr : partial, st);
+  return qb200_gemm_run(gp, epi, g, st);
+}
+
 // Every layer of a step plus the final RMSNorm (w.norm16 feeds the lm_head).
 int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, const int *tokens_in,
                 float *norm_out, int max_position, float attn_scale, cudaStream_t st) {
@@ -732,7 +785,7 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     g.pdl = 1;
     g.out = w.qkv;
     g.ldo = QKV;
-    if (int rc = qb200_gemm_run(p->g_qkv[l], qb200tc::EPI_F16, g, st)) return rc;
+    if (int rc = run_proj(p, 0, p->g_qkv[l], qb200tc::EPI_F16, g, w.splitk, st)) return rc;
     LAUNCH(qk_rope_kv_kernel, dim3(rows), dim3(256), 0, static_cast<const __half *>(w.qkv),
            static_cast<const __half *>(L.q_norm), static_cast<const __half *>(L.k_norm), p->cos_t,
            p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->kg, p->max_seq,
@@ -746,19 +799,17 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     g.out = w.act;
     g.ldo = H;
     g.res = w.hidden;
-    if (int rc = qb200_gemm_run_splitk(p->g_o[l], qb200tc::EPI_F32_RES16, g, KSPLIT, w.splitk, st))
-      return rc;
+    if (int rc = run_proj(p, 1, p->g_o[l], qb200tc::EPI_F32_RES16, g, w.splitk, st)) return rc;
     LAUNCH(post_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const float *>(w.act),
            static_cast<const __half *>(L.post_norm), w.sact, rows);
     g.out = w.inter;
     g.ldo = IM;
     g.res = nullptr;
-    if (int rc = qb200_gemm_run(p->g_gu[l], qb200tc::EPI_SWIGLU, g, st)) return rc;
+    if (int rc = run_proj(p, 2, p->g_gu[l], qb200tc::EPI_SWIGLU, g, w.splitk, st)) return rc;
     g.out = w.hidden;
     g.ldo = H;
     g.res = w.act;
-    if (int rc = qb200_gemm_run_splitk(p->g_down[l], qb200tc::EPI_F16_RES32, g, KSPLIT, w.splitk, st))
-      return rc;
+    if (int rc = run_proj(p, 3, p->g_down[l], qb200tc::EPI_F16_RES32, g, w.splitk, st)) return rc;
   }
   LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const __half *>(w.hidden),
          p->final_norm, w.norm16, norm_out, rows);

@@ -71,7 +71,12 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
   }
   const float a[4] = {acc.x, acc.y, acc.z, acc.w};
   const size_t o = static_cast<size_t>(row) * ldo + col;
-  if (epi == EPI_F32_RES16) {
+  if (epi == EPI_SWIGLU) {
+    // Column pairs (gate, up) -> output column col / 2 (ldo counts outputs).
+    __half *out16 = static_cast<__half *>(out) + static_cast<size_t>(row) * ldo + col / 2;
+    out16[0] = __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(a[0]))), a[1]));
+    out16[1] = __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(a[2]))), a[3]));
+  } else if (epi == EPI_F32_RES16) {
     const __half *r = static_cast<const __half *>(res) + o;
     float4 w;
     w.x = __fadd_rn(a[0], __half2float(r[0]));
@@ -153,7 +158,7 @@ using namespace qb200tc;
 namespace {
 
 std::mutex g_mu;
-bool g_attr[64][2][7] = {};
+bool g_attr[64][3][8][3] = {};  // [device][BN 64/128/256][epilogue][B layout]
 
 int fail(int code, const char *fmt, ...) {
   char buf[512];
@@ -164,16 +169,17 @@ int fail(int code, const char *fmt, ...) {
   return qb200_set_error(code, buf);
 }
 
-template <int BN, int EPI>
-int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, cudaStream_t st) {
+template <int BN, int EPI, int BL = BL_K>
+int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mb2, const GemmArgs &g,
+             cudaStream_t st) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(2, "cudaGetDevice failed");
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    bool &done = g_attr[dev][BN == 128][EPI];
+    bool &done = g_attr[dev][BN == 64 ? 0 : (BN == 128 ? 1 : 2)][EPI][BL];
     if (!done) {
       const cudaError_t e = cudaFuncSetAttribute(
-          gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          gemm_tc_kernel<BN, EPI, BL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
           static_cast<int>(GemmSmem<BN>::bytes(GemmSmem<BN>::MAX_STAGES)));
       if (e != cudaSuccess) return fail(4, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       done = true;
@@ -185,9 +191,9 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g, cu
   GemmArgs ga = g;
   const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
   ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
-  const cudaError_t e = qb200_launch_cl(gemm_tc_kernel<BN, EPI>, grid, dim3(THREADS),
+  const cudaError_t e = qb200_launch_cl(gemm_tc_kernel<BN, EPI, BL>, grid, dim3(THREADS),
                                         GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0,
-                                        ga.cluster_k ? static_cast<int>(grid.z) : 1, ma, mb, ga);
+                                        ga.cluster_k ? static_cast<int>(grid.z) : 1, ma, mb, mb2, ga);
   if (e != cudaSuccess) return fail(20, "GEMM launch: %s", cudaGetErrorString(e));
   return 0;
 }
@@ -196,14 +202,29 @@ template <int BN>
 int launch_bn(int epi, const CUtensorMap &ma, const CUtensorMap &mb, const GemmArgs &g,
               cudaStream_t st) {
   switch (epi) {
-    case EPI_F16: return launch_t<BN, EPI_F16>(ma, mb, g, st);
-    case EPI_F32: return launch_t<BN, EPI_F32>(ma, mb, g, st);
-    case EPI_F32_RES16: return launch_t<BN, EPI_F32_RES16>(ma, mb, g, st);
-    case EPI_SWIGLU: return launch_t<BN, EPI_SWIGLU>(ma, mb, g, st);
-    case EPI_F16_RES32: return launch_t<BN, EPI_F16_RES32>(ma, mb, g, st);
-    case EPI_ARGMAX: return launch_t<BN, EPI_ARGMAX>(ma, mb, g, st);
-    case EPI_PARTIAL: return launch_t<BN, EPI_PARTIAL>(ma, mb, g, st);
+    case EPI_F16: return launch_t<BN, EPI_F16>(ma, mb, mb, g, st);
+    case EPI_F32: return launch_t<BN, EPI_F32>(ma, mb, mb, g, st);
+    case EPI_F32_RES16: return launch_t<BN, EPI_F32_RES16>(ma, mb, mb, g, st);
+    case EPI_SWIGLU: return launch_t<BN, EPI_SWIGLU>(ma, mb, mb, g, st);
+    case EPI_F16_RES32: return launch_t<BN, EPI_F16_RES32>(ma, mb, mb, g, st);
+    case EPI_ARGMAX: return launch_t<BN, EPI_ARGMAX>(ma, mb, mb, g, st);
+    case EPI_PARTIAL: return launch_t<BN, EPI_PARTIAL>(ma, mb, mb, g, st);
     default: return fail(10, "unknown epilogue %d", epi);
+  }
+}
+
+// MN-major B: the plain projection (EPI_F16, optional bias; split-K inside a
+// cluster) and the gate|up pair (EPI_SWIGLU2, BN = 128).
+template <int BN>
+int launch_bn_mn(int epi, const GemmPlan &p, const GemmArgs &g, cudaStream_t st) {
+  if (p.bl == BL_MN2) {
+    if (epi != EPI_SWIGLU2 || BN != 128) return fail(10, "the gate|up layout takes EPI_SWIGLU2 at BN 128");
+    return launch_t<128, EPI_SWIGLU2, BL_MN2>(p.ma, p.mb, p.mb2, g, st);
+  }
+  switch (epi) {
+    case EPI_F16: return launch_t<BN, EPI_F16, BL_MN>(p.ma, p.mb, p.mb, g, st);
+    case EPI_F32: return launch_t<BN, EPI_F32, BL_MN>(p.ma, p.mb, p.mb, g, st);
+    default: return fail(10, "epilogue %d is not built for an MN-major B", epi);
   }
 }
 
@@ -227,6 +248,8 @@ int qb200_gemm_make_maps(GemmPlan *p, const void *a, const void *b, int M, int N
   p->N = N;
   p->K = K;
   p->bn = qb200_gemm_bn(M, N);
+  p->b_ptr = b;
+  p->ldb = ldb;
   if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, BM, 1)) return rc;
   if (int rc = qb200_encode_f16_2d(&p->mb, b, K, N, ldb, BK, p->bn, 1)) return rc;
   return 0;
@@ -237,14 +260,51 @@ int qb200_gemm_run(const GemmPlan &p, int epi, GemmArgs g, cudaStream_t st) {
   g.N = p.N;
   g.K = p.K;
   g.n_tiles = (p.N + p.bn - 1) / p.bn;
+  if (p.bl != BL_K)
+    return p.bn == 128 ? launch_bn_mn<128>(epi, p, g, st) : launch_bn_mn<64>(epi, p, g, st);
+  if (p.bn == 256) return launch_bn<256>(epi, p.ma, p.mb, g, st);
   return p.bn == 128 ? launch_bn<128>(epi, p.ma, p.mb, g, st) : launch_bn<64>(epi, p.ma, p.mb, g, st);
+}
+
+int qb200_gemm_set_bn(GemmPlan *p, int bn) {
+  if (p->bl != BL_K || (bn != 64 && bn != 128 && bn != 256))
+    return fail(10, "tile width %d: 64, 128 or 256 columns (K-major B only)", bn);
+  p->bn = bn;
+  // The B tensor map's box height is the tile width.
+  return qb200_encode_f16_2d(&p->mb, p->b_ptr, p->K, p->N, p->ldb, BK, bn, 1);
+}
+
+int qb200_gemm_make_maps_mn(GemmPlan *p, const void *a, const void *b, const void *b2, int M, int N,
+                            int K, int lda, int ldb, int bn, int b_rows) {
+  if (b_rows <= 0) b_rows = K;
+  const int n_cols = b2 != nullptr ? 2 * N : N;  // gate|up: the accumulator holds both
+  if (M < 1 || N < 64 || K < BK || (N & 63) || (K % BK) || b_rows < BK || (b_rows % BK))
+    return fail(10, "GEMM shape M=%d N=%d K=%d: need N a multiple of 64 and K a multiple of %d", M, N,
+                K, BK);
+  if (!al16(a) || !al16(b) || (b2 != nullptr && !al16(b2)) || (lda & 7) || (ldb & 7))
+    return fail(14, "GEMM operands must be 16-byte aligned with row pitches a multiple of 8");
+  if (b2 != nullptr && bn != 128) return fail(10, "the gate|up layout needs 128-column tiles");
+  p->M = M;
+  p->N = n_cols;
+  p->K = K;
+  p->bn = bn;
+  p->bl = b2 != nullptr ? BL_MN2 : BL_MN;
+  if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, BM, 1)) return rc;
+  // B stored [K, N] (N contiguous): boxes of 64 columns x BK rows, 128-byte swizzle.
+  if (int rc = qb200_encode_f16_2d(&p->mb, b, N, b_rows, ldb, 64, BK, 1)) return rc;
+  if (b2 != nullptr) {
+    if (int rc = qb200_encode_f16_2d(&p->mb2, b2, N, b_rows, ldb, 64, BK, 1)) return rc;
+  } else {
+    p->mb2 = p->mb;
+  }
+  return 0;
 }
 
 int qb200_gemm_run_splitk(const GemmPlan &p, int epi, GemmArgs g, int splits, float *partial,
                           cudaStream_t st) {
   const int nk = p.K / BK;
   if (splits < 2 || splits > nk) return fail(10, "k_splits=%d out of range [2, %d]", splits, nk);
-  if (epi != EPI_F16 && epi != EPI_F32 && epi != EPI_F32_RES16 && epi != EPI_F16_RES32)
+  if (epi != EPI_F16 && epi != EPI_F32 && epi != EPI_F32_RES16 && epi != EPI_F16_RES32 && epi != EPI_SWIGLU)
     return fail(10, "epilogue %d cannot follow a split-K reduction", epi);
   if (splits <= 8 && partial == nullptr) {
     // The k slices of a tile form one cluster and are added in shared memory.
@@ -330,6 +390,13 @@ long long qwen_b200_gemm_argmax_workspace(int M, int N) {
 
 int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, const void *res,
                        void *workspace, int M, int N, int K, int ldo, int k_splits, void *stream) {
+  return qwen_b200_gemm_f16_tiled(epilogue, a, b, out, res, workspace, M, N, K, ldo, k_splits, 0,
+                                  stream);
+}
+
+int qwen_b200_gemm_f16_tiled(int epilogue, const void *a, const void *b, void *out, const void *res,
+                             void *workspace, int M, int N, int K, int ldo, int k_splits, int bn,
+                             void *stream) {
   qb200_clear_error();
   if (a == nullptr || b == nullptr || out == nullptr) return fail(13, "null pointer argument");
   if (epilogue < 0 || epilogue > EPI_ARGMAX) return fail(10, "unknown epilogue %d", epilogue);
@@ -339,6 +406,10 @@ int qwen_b200_gemm_f16(int epilogue, const void *a, const void *b, void *out, co
   if (k_splits > 8 && workspace == nullptr) return fail(13, "more than 8 k slices need a workspace");
   GemmPlan p{};
   if (int rc = qb200_gemm_make_maps(&p, a, b, M, N, K, K, K)) return rc;
+  if (bn != 0) {
+    if (epilogue == EPI_ARGMAX) return fail(10, "the argmax epilogue takes the default tile width");
+    if (int rc = qb200_gemm_set_bn(&p, bn)) return rc;
+  }
   GemmArgs g{};
   g.ldo = epilogue == EPI_SWIGLU ? N / 2 : (epilogue == EPI_ARGMAX ? 1 : ldo);
   if (epilogue != EPI_ARGMAX && epilogue != EPI_SWIGLU && ldo < N)

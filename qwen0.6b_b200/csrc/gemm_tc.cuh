@@ -2,7 +2,9 @@
 // fused epilogues of the batched decode layer.
 //
 //   C[M, N] = A[M, K] . B[N, K]^T      A, B fp16 K-major (row-major [rows, K]),
-//                                       fp32 accumulation in tensor memory.
+//                                       fp32 accumulation in tensor memory;
+//   or, with an MN-major B (the weight stored [K, N], N contiguous, as the
+//   upstream Tools/swiglu operators keep it), C[M, N] = A[M, K] . B[K, N].
 //
 // One CTA computes one 128 x BN tile over the whole K range:
 //   warp 0      one lane streams A/B k-blocks (128 / BN rows x 64 halves) into a
@@ -39,7 +41,7 @@ constexpr int BK = 64;                 // 64 halves = one 128-byte swizzle row
 // larger than the GPU.
 template <int BN>
 constexpr int max_stages() {
-  return BN == 64 ? 8 : 6;
+  return BN == 64 ? 8 : (BN == 128 ? 6 : 4);  // 24 / 32 / 48 KB stages
 }
 constexpr int THREADS = 192;           // 6 warps
 constexpr long long WAIT_NS = 2000000000LL;
@@ -53,6 +55,19 @@ enum Epilogue : int {
   EPI_F16_RES32 = 4,   // out16[r, c] = half(acc + res32[r, c])            (down + residual)
   EPI_ARGMAX = 5,      // part_val/part_idx[r, tile] = max / lowest argmax over the tile's columns
   EPI_PARTIAL = 6,     // split-K: out32[z, r, c] = this CTA's partial sum over its k-range z
+  EPI_SWIGLU2 = 7,     // BL_MN2: accumulator columns [0, BN/2) = gate, [BN/2, BN) = up of the
+                       //   same BN/2 outputs: g = acc + bias[c], u = acc + bias2[c] (fp32),
+                       //   out16[r, c] = half(s), s = g / (1 + exp(-g)) * u, and with lo_col the
+                       //   rounding residual half(s - half(s)) at column lo_col + c (so a following
+                       //   GEMM over [hi | lo] with B's K wrapped sees s to ~22 bits); out2 / out3
+                       //   (if set) = half(g), half(u)
+};
+
+// Layout of the B operand in global memory (and so in shared memory).
+enum BLayout : int {
+  BL_K = 0,    // [N, K] K-major; the tile is one 128-byte-swizzled TMA box
+  BL_MN = 1,   // [K, N] MN-major; BN / 64 boxes of 64 columns x BK rows
+  BL_MN2 = 2,  // two [K, N] MN-major matrices (gate, up): 64 columns of each (BN = 128)
 };
 
 struct GemmArgs {
@@ -68,6 +83,11 @@ struct GemmArgs {
   int cluster_k;                // split-K reduced inside a (1, 1, k_splits) cluster (see below)
   int pdl;                      // host side: launch as a programmatic dependent of the previous kernel
   unsigned long long *err;      // status word (nullptr: none)
+  const void *bias;             // fp16 [N] added before rounding (EPI_F16, EPI_SWIGLU2 gate) or nullptr
+  const void *bias2;            // fp16 [N] up bias of EPI_SWIGLU2 or nullptr
+  void *out2, *out3;            // EPI_SWIGLU2: fp16 gate / up caches [M, ldo] or nullptr
+  int lo_col;                   // EPI_SWIGLU2: > 0: also out16[r, lo_col + c] = half(s - half(s))
+  int b_kwrap;                  // > 0: B's K coordinate wraps after this many k-blocks
 };
 
 template <int BN>
@@ -100,11 +120,25 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: A, B fp16, D fp32, both K-major, M=128.
+// MN-major operand, 128-byte swizzle: each K row of 64 MN elements is 128 B,
+// 8-row atoms are 1024 B apart (stride dimension), and the 64-element MN
+// blocks are `lbo` bytes apart (leading dimension).
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);        // start address
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;      // LBO: next 64-element MN block
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;                 // SBO: next 8-row K atom
+  d |= static_cast<uint64_t>(1u) << 46;                         // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                         // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: A, B fp16, D fp32, A K-major, M=128; B
+// K-major, or MN-major ("transpose B", bit 16) when b_mn.
 template <int BN>
-__device__ __forceinline__ constexpr uint32_t idesc_f16() {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
-         (static_cast<uint32_t>(BM >> 4) << 24);
+__device__ __forceinline__ constexpr uint32_t idesc_f16(bool b_mn = false) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (b_mn ? (1u << 16) : 0u) |
+         (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -221,11 +255,13 @@ __device__ __forceinline__ __half silu_half(__half x) {
   return __hmul_rn(x, r);
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int BL = BL_K>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tm_b2, const GemmArgs g) {
   using S = GemmSmem<BN>;
+  static_assert(BL != BL_MN2 || (BN == 128 && EPI == EPI_SWIGLU2), "gate|up tiles are 64 + 64 columns");
+  static_assert(EPI != EPI_SWIGLU2 || BL == BL_MN2, "EPI_SWIGLU2 needs the gate|up B layout");
   const int STAGES = g.stages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -238,7 +274,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Split-K reduced in the cluster (launched with cluster dims (1, 1, k_splits)).
-  constexpr bool CAN_CLUSTER = EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_F32_RES16 || EPI == EPI_F16_RES32;
+  constexpr bool CAN_CLUSTER = EPI == EPI_F16 || EPI == EPI_F32 || EPI == EPI_F32_RES16 ||
+                               EPI == EPI_F16_RES32 || EPI == EPI_SWIGLU;
   const bool clustered = CAN_CLUSTER && g.cluster_k != 0 && gridDim.z > 1;
   constexpr int TPITCH = BN + 4;  // fp32 partial tile row pitch (16-byte shift per row)
   const int nk_all = (g.K + BK - 1) / BK;
@@ -246,6 +283,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int kb0 = static_cast<int>((static_cast<long long>(nk_all) * blockIdx.z) / gridDim.z);
   const int nk = static_cast<int>((static_cast<long long>(nk_all) * (blockIdx.z + 1)) / gridDim.z) - kb0;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // B tile of k-block kb into dst (one k-block: BK rows of K).  MN-major:
+  // boxes of 64 columns x BK rows, each BK * 128 bytes; BL_MN2 takes the
+  // gate and the up columns [n0 / 2, n0 / 2 + 64) of the two matrices.
+  auto load_b = [&](uint8_t *dst, int kb, uint64_t *bar) {
+    if (g.b_kwrap > 0) kb %= g.b_kwrap;
+    if constexpr (BL == BL_K) {
+      tma_load_2d(dst, &tm_b, kb * BK, n0, bar);
+    } else if constexpr (BL == BL_MN) {
+#pragma unroll
+      for (int j = 0; j < BN / 64; ++j) tma_load_2d(dst + j * BK * 128, &tm_b, n0 + 64 * j, kb * BK, bar);
+    } else {
+      tma_load_2d(dst, &tm_b, n0 / 2, kb * BK, bar);
+      tma_load_2d(dst + BK * 128, &tm_b2, n0 / 2, kb * BK, bar);
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -274,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int kb = 0; kb < pre; ++kb) {
         uint8_t *st = base + kb * S::STAGE;
         mbar_arrive_expect_tx(&full[kb], S::STAGE);
-        tma_load_2d(st + S::A_BYTES, &tm_b, (kb0 + kb) * BK, n0, &full[kb]);
+        load_b(st + S::A_BYTES, kb0 + kb, &full[kb]);
       }
       qb200::griddep_wait();
       for (int kb = 0; kb < pre; ++kb)
@@ -286,7 +338,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t *st = base + s * S::STAGE;
         mbar_arrive_expect_tx(&full[s], S::STAGE);
         tma_load_2d(st, &tm_a, (kb0 + kb) * BK, m0, &full[s]);
-        tma_load_2d(st + S::A_BYTES, &tm_b, (kb0 + kb) * BK, n0, &full[s]);
+        load_b(st + S::A_BYTES, kb0 + kb, &full[s]);
         issued = kb + 1;
       }
       // Every issued copy lands before the CTA may exit (matters after an abort).
@@ -301,7 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16<BN>();
+      constexpr uint32_t idesc = idesc_f16<BN>(BL != BL_K);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % STAGES;
         if (!gemm_wait(&full[s], (kb / STAGES) & 1, abort, g.err, 2)) break;
@@ -309,9 +361,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t sa = smem_u32(base + s * S::STAGE);
         const uint32_t sb = sa + S::A_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          mma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc,
-                  (kb | k) != 0 ? 1u : 0u);
+        for (int k = 0; k < BK / 16; ++k) {
+          // K-major B advances 16 elements (32 bytes) along its rows; MN-major
+          // B advances 16 rows (two 1024-byte atoms).
+          const uint64_t bd = BL == BL_K ? sw128_desc(sb + 32 * k) : sw128_mn_desc(sb + 2048 * k, BK * 128);
+          mma_f16(tmem, sw128_desc(sa + 32 * k), bd, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
         mma_commit(&empty[s]);
       }
       // Signals the accumulator once every MMA issued above has completed
@@ -340,6 +395,48 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < 4; ++i)
           reinterpret_cast<float4 *>(trow + c0)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
+    } else if (ok && EPI == EPI_SWIGLU2) {
+      // Columns c of the gate half and c + BN/2 of the up half are output
+      // column n0 / 2 + c.
+      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
+      const int nout = g.N / 2;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+        float gv[16], uv[16];
+        tmem_ld16(tq + c0, gv);
+        tmem_ld16(tq + BN / 2 + c0, uv);
+        const int col = n0 / 2 + c0;
+        if (row >= g.M || col >= nout) continue;
+        const int nvalid = min(16, nout - col);
+        const size_t o = static_cast<size_t>(row) * g.ldo + col;
+        __half *out = static_cast<__half *>(g.out) + o;
+        __align__(16) __half hv[16], lv[16], gh[16], uh[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const bool in = i < nvalid;
+          const float gg = (g.bias != nullptr && in) ? __fadd_rn(gv[i], __half2float(static_cast<const __half *>(g.bias)[col + i])) : gv[i];
+          const float uu = (g.bias2 != nullptr && in) ? __fadd_rn(uv[i], __half2float(static_cast<const __half *>(g.bias2)[col + i])) : uv[i];
+          const float sv = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
+          hv[i] = __float2half_rn(sv);
+          lv[i] = __float2half_rn(__fsub_rn(sv, __half2float(hv[i])));
+          gh[i] = __float2half_rn(gg);
+          uh[i] = __float2half_rn(uu);
+        }
+        // 16-byte stores when the 16 columns are whole (ldo, lo_col and col
+        // are multiples of 8 on the planned shapes), else element by element.
+        auto put = [&](__half *dst, const __half (&src)[16]) {
+          if (nvalid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            reinterpret_cast<uint4 *>(dst)[0] = reinterpret_cast<const uint4 *>(src)[0];
+            reinterpret_cast<uint4 *>(dst)[1] = reinterpret_cast<const uint4 *>(src)[1];
+          } else {
+            for (int i = 0; i < nvalid; ++i) dst[i] = src[i];
+          }
+        };
+        put(out, hv);
+        if (g.lo_col > 0) put(out + g.lo_col, lv);
+        if (g.out2 != nullptr) put(static_cast<__half *>(g.out2) + o, gh);
+        if (g.out3 != nullptr) put(static_cast<__half *>(g.out3) + o, uh);
+      }
     } else if (ok) {
       const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
       float best = -INFINITY;
@@ -354,6 +451,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int nvalid = min(16, g.N - col);
         if constexpr (EPI == EPI_F16) {
           __half *out = static_cast<__half *>(g.out) + o;
+          if (g.bias != nullptr) {
+            const __half *b = static_cast<const __half *>(g.bias) + col;
+            for (int i = 0; i < nvalid; ++i) v[i] = __fadd_rn(v[i], __half2float(b[i]));
+          }
           if (nvalid == 16) {
             uint4 pk[2];
             __half2 *h = reinterpret_cast<__half2 *>(pk);
@@ -389,10 +490,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else if constexpr (EPI == EPI_SWIGLU) {
           // ldo counts output columns (inter); column pair (2i, 2i+1) -> output i.
           __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
-          for (int i = 0; i + 1 < nvalid; i += 2) {
-            const float gate = v[i], up = v[i + 1];
-            const float act = __fmul_rn(__half2float(silu_half(__float2half_rn(gate))), up);
-            out[i / 2] = __float2half_rn(act);
+          __align__(16) __half act[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            act[i] = __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(v[2 * i]))), v[2 * i + 1]));
+          if (nvalid == 16 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+            *reinterpret_cast<uint4 *>(out) = *reinterpret_cast<const uint4 *>(act);
+          } else {
+            for (int i = 0; i + 1 < nvalid; i += 2) out[i / 2] = act[i / 2];
           }
         } else if constexpr (EPI == EPI_ARGMAX) {
           for (int i = 0; i < nvalid; ++i)
@@ -413,44 +518,68 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_before();
   __syncthreads();
   if (clustered) {
-    // Split-K reduced inside the cluster: rank 0 adds the k slices' partial
-    // tiles in slice order (as the separate reduction kernel adds its slices),
+    // Split-K reduced inside the cluster: every rank adds the k slices'
+    // partial tiles for its share of the tile's rows, in slice order (as the
+    // separate reduction kernel adds its slices, so the bits are the same),
     // then applies the epilogue.  Every thread of every CTA takes both
     // cluster barriers, also after an abort.
     cluster_sync_all();
-    if (cluster_rank() == 0 && warp >= 2) {
-      const int q = warp & 3, lrow = 32 * q + lane, row = m0 + lrow;
-      const uint32_t trow = smem_u32(base) + static_cast<uint32_t>(lrow * TPITCH) * 4u;
-      if (row < g.M && !*abort) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 4) {
-          const int col = n0 + c;
-          if (col >= g.N) break;
-          float4 acc = ld_dsmem_f4(map_rank(trow + c * 4, 0));
-          for (uint32_t z = 1; z < gridDim.z; ++z) {
-            const float4 v = ld_dsmem_f4(map_rank(trow + c * 4, z));
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+    const int Z = static_cast<int>(gridDim.z);
+    const int rank = static_cast<int>(cluster_rank());
+    const int rows_per = (BM + Z - 1) / Z;
+    const int r0 = rank * rows_per, r1 = min(BM, r0 + rows_per);
+    if (warp >= 2 && !*abort) {
+      constexpr int C4 = BN / 4;
+      const int t = threadIdx.x - 64;  // 0..127
+      for (int idx = t; idx < (r1 - r0) * C4; idx += 128) {
+        const int lrow = r0 + idx / C4, c = 4 * (idx % C4);
+        const int row = m0 + lrow, col = n0 + c;
+        if (row >= g.M || col >= g.N) continue;
+        const uint32_t trow = smem_u32(base) + static_cast<uint32_t>(lrow * TPITCH) * 4u;
+        float4 pz[8];
+#pragma unroll
+        for (int z = 0; z < 8; ++z)
+          if (z < Z) pz[z] = ld_dsmem_f4(map_rank(trow + c * 4, z));
+        float4 acc = pz[0];
+#pragma unroll
+        for (int z = 1; z < 8; ++z) {
+          if (z < Z) {
+            acc.x = __fadd_rn(acc.x, pz[z].x);
+            acc.y = __fadd_rn(acc.y, pz[z].y);
+            acc.z = __fadd_rn(acc.z, pz[z].z);
+            acc.w = __fadd_rn(acc.w, pz[z].w);
           }
-          const size_t o = static_cast<size_t>(row) * g.ldo + col;
-          if constexpr (EPI == EPI_F32_RES16) {
-            const __half *r = static_cast<const __half *>(g.res) + o;
-            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) =
-                make_float4(__fadd_rn(acc.x, __half2float(r[0])), __fadd_rn(acc.y, __half2float(r[1])),
-                            __fadd_rn(acc.z, __half2float(r[2])), __fadd_rn(acc.w, __half2float(r[3])));
-          } else if constexpr (EPI == EPI_F16_RES32) {
-            const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(g.res) + o);
-            __half2 h[2] = {__floats2half2_rn(__fadd_rn(acc.x, r.x), __fadd_rn(acc.y, r.y)),
-                            __floats2half2_rn(__fadd_rn(acc.z, r.z), __fadd_rn(acc.w, r.w))};
-            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
-          } else if constexpr (EPI == EPI_F32) {
-            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) = acc;
-          } else if constexpr (EPI == EPI_F16) {
-            __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
-            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+        }
+        const size_t o = static_cast<size_t>(row) * g.ldo + col;
+        if constexpr (EPI == EPI_F32_RES16) {
+          const __half *r = static_cast<const __half *>(g.res) + o;
+          *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) =
+              make_float4(__fadd_rn(acc.x, __half2float(r[0])), __fadd_rn(acc.y, __half2float(r[1])),
+                          __fadd_rn(acc.z, __half2float(r[2])), __fadd_rn(acc.w, __half2float(r[3])));
+        } else if constexpr (EPI == EPI_F16_RES32) {
+          const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(g.res) + o);
+          __half2 h[2] = {__floats2half2_rn(__fadd_rn(acc.x, r.x), __fadd_rn(acc.y, r.y)),
+                          __floats2half2_rn(__fadd_rn(acc.z, r.z), __fadd_rn(acc.w, r.w))};
+          *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+        } else if constexpr (EPI == EPI_F32) {
+          *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) = acc;
+        } else if constexpr (EPI == EPI_SWIGLU) {
+          // Column pairs (gate, up) -> output column col / 2 (ldo counts outputs).
+          __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
+          __half2 h = __halves2half2(
+              __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.x))), acc.y)),
+              __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.z))), acc.w)));
+          *reinterpret_cast<__half2 *>(out) = h;
+        } else if constexpr (EPI == EPI_F16) {
+          if (g.bias != nullptr) {
+            const __half *b = static_cast<const __half *>(g.bias) + col;
+            acc.x = __fadd_rn(acc.x, __half2float(b[0]));
+            acc.y = __fadd_rn(acc.y, __half2float(b[1]));
+            acc.z = __fadd_rn(acc.z, __half2float(b[2]));
+            acc.w = __fadd_rn(acc.w, __half2float(b[3]));
           }
+          __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
+          *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
         }
       }
     }

@@ -38,6 +38,7 @@
 
 #include <mutex>
 
+#include "gemm_tc_host.h"
 #include "host_err.h"
 #include "launch.h"
 #include "ptx.cuh"
@@ -528,6 +529,46 @@ int down_launch(const void *s, const void *wd, const void *bd, void *out, long l
   return launch_chain<false>(static_cast<const __half *>(s), wdh, wdh, a, st);
 }
 
+// Rows from which the dispatching entry points take the tensor-core path.
+constexpr long long TC_MIN_ROWS = 64;
+
+bool tc_shape_ok(int hidden, int inter) { return hidden % 64 == 0 && inter % 64 == 0 && hidden >= 64; }
+
+// s[rows, inter] = silu(g) * u, g = x . w_gate + b_gate, u = x . w_up + b_up in
+// fp32, then out[rows, hidden] = half(s . w_down + b_down): two tcgen05 GEMMs
+// with fp32 accumulation on the upstream [K, N] weight layout (MN-major B).
+// The gate|up GEMM holds 64 gate and 64 up columns per 128-column tile and
+// stores s as fp16 hi = half(s) and lo = half(s - hi) ([rows, 2 inter] in
+// sbuf); the down GEMM runs over K = 2 inter ([hi | lo] against w_down read
+// twice), so s enters it with ~22 significant bits, and splits K over a
+// thread-block cluster (no workspace).
+int swiglu_down_tc(const void *x, const void *wg, const void *wu, const void *wd, const void *bg,
+                   const void *bu, const void *bd, void *sbuf, void *out, long long rows, int hidden,
+                   int inter, cudaStream_t st) {
+  const int M = static_cast<int>(rows);
+  GemmPlan p1{};
+  if (int rc = qb200_gemm_make_maps_mn(&p1, x, wg, wu, M, inter, hidden, hidden, inter, 128)) return rc;
+  qb200tc::GemmArgs g1{};
+  g1.out = sbuf;
+  g1.ldo = 2 * inter;
+  g1.lo_col = inter;
+  g1.bias = bg;
+  g1.bias2 = bu;
+  if (int rc = qb200_gemm_run(p1, qb200tc::EPI_SWIGLU2, g1, st)) return rc;
+  GemmPlan p2{};
+  if (int rc = qb200_gemm_make_maps_mn(&p2, sbuf, wd, nullptr, M, hidden, 2 * inter, 2 * inter, hidden,
+                                       64, inter))
+    return rc;
+  qb200tc::GemmArgs g2{};
+  g2.out = out;
+  g2.ldo = hidden;
+  g2.bias = bd;
+  g2.b_kwrap = inter / qb200tc::BK;
+  const int tiles = (hidden / 64) * ((M + qb200tc::BM - 1) / qb200tc::BM);
+  const int splits = tiles >= 32 ? 4 : 8;
+  return qb200_gemm_run_splitk(p2, qb200tc::EPI_F16, g2, splits, nullptr, st);
+}
+
 }  // namespace
 
 // 2-D fp16 tensor [outer, inner] with row pitch `pitch` elements, box
@@ -577,7 +618,7 @@ int qwen_b200_swiglu_forward(const void *x, const void *w_gate, const void *w_up
 
 long long qwen_b200_swiglu_forward_down_workspace(long long rows, int inter) {
   if (rows < 0 || inter < 0) return 0;
-  return round256(rows * inter * 2);
+  return round256(rows * inter * 4);  // fp16 s (chains) or its hi | lo parts (tensor cores)
 }
 
 int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void *w_up,
@@ -598,9 +639,65 @@ int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void 
   return down_launch(workspace, w_down, b_down, out, rows, hidden, inter, st);
 }
 
+int qwen_b200_swiglu_forward_down_ex(const void *x, const void *w_gate, const void *w_up,
+                                     const void *w_down, const void *b_gate, const void *b_up,
+                                     const void *b_down, void *out, void *workspace,
+                                     long long rows, int hidden, int inter, int mode, void *stream) {
+  qb200_clear_error();
+  if (mode < -1 || mode > 1) return fail(10, "mode=%d: -1 (by size), 0 (tensor cores) or 1 (exact)", mode);
+  const bool tc = mode == 0 || (mode == -1 && rows >= TC_MIN_ROWS && tc_shape_ok(hidden, inter));
+  if (!tc) return qwen_b200_swiglu_forward_down(x, w_gate, w_up, w_down, b_gate, b_up, b_down, out,
+                                                workspace, rows, hidden, inter, stream);
+  if (int rc = check_swiglu(x, w_gate, w_up, w_down, b_gate, b_up, b_down, rows, hidden, inter))
+    return rc;
+  if (rows == 0) return 0;
+  if (!tc_shape_ok(hidden, inter))
+    return fail(10, "the tensor-core path needs hidden and inter multiples of 64 (got %d, %d)", hidden, inter);
+  if (rows > 0x7fffffffll) return fail(10, "rows=%lld out of range", rows);
+  if (w_down == nullptr || out == nullptr || workspace == nullptr)
+    return fail(13, "null pointer argument");
+  if (!al16(out) || !al16(workspace)) return fail(14, "SwiGLU operands must be 16-byte aligned");
+  return swiglu_down_tc(x, w_gate, w_up, w_down, b_gate, b_up, b_down, workspace, out, rows, hidden,
+                        inter, static_cast<cudaStream_t>(stream));
+}
+
+int qwen_b200_rmsnorm_swiglu_down_ex(const void *x, const void *norm_weight, void *residual,
+                                     float eps, const void *w_gate, const void *w_up,
+                                     const void *w_down, const void *b_gate, const void *b_up,
+                                     const void *b_down, void *normed, float *rms, void *out,
+                                     void *workspace, long long rows, int hidden, int inter, int mode,
+                                     void *stream) {
+  qb200_clear_error();
+  if (mode < -1 || mode > 1) return fail(10, "mode=%d: -1 (by size), 0 (tensor cores) or 1 (exact)", mode);
+  const bool tc = mode == 0 || (mode == -1 && rows >= TC_MIN_ROWS && tc_shape_ok(hidden, inter));
+  if (!tc) return qwen_b200_rmsnorm_swiglu_down(x, norm_weight, residual, eps, w_gate, w_up, w_down,
+                                                b_gate, b_up, b_down, normed, rms, out, workspace,
+                                                rows, hidden, inter, stream);
+  if (int rc = check_swiglu(x, w_gate, w_up, w_down, b_gate, b_up, b_down, rows, hidden, inter))
+    return rc;
+  if (rows == 0) return 0;
+  if (!tc_shape_ok(hidden, inter))
+    return fail(10, "the tensor-core path needs hidden and inter multiples of 64 (got %d, %d)", hidden, inter);
+  if (rows > 0x7fffffffll) return fail(10, "rows=%lld out of range", rows);
+  if (norm_weight == nullptr || w_down == nullptr || rms == nullptr || out == nullptr ||
+      workspace == nullptr)
+    return fail(13, "null pointer argument");
+  for (const void *q : {norm_weight, static_cast<const void *>(residual),
+                        static_cast<const void *>(normed), static_cast<const void *>(out),
+                        static_cast<const void *>(workspace)})
+    if (q != nullptr && !al16(q)) return fail(14, "operands must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  void *nbuf = normed != nullptr ? normed : ws;
+  void *sbuf = ws + round256(rows * hidden * 2);
+  if (int rc = rmsnorm_launch(nbuf, rms, x, norm_weight, residual, rows, hidden, eps, st)) return rc;
+  return swiglu_down_tc(nbuf, w_gate, w_up, w_down, b_gate, b_up, b_down, sbuf, out, rows, hidden,
+                        inter, st);
+}
+
 long long qwen_b200_rmsnorm_swiglu_down_workspace(long long rows, int hidden, int inter) {
   if (rows < 0 || hidden < 0 || inter < 0) return 0;
-  return round256(rows * hidden * 2) + round256(rows * inter * 2);
+  return round256(rows * hidden * 2) + round256(rows * inter * 4);
 }
 
 int qwen_b200_rmsnorm_swiglu_down(const void *x, const void *norm_weight, void *residual,

@@ -10,6 +10,11 @@
 //     -> [out, normed, rms]  (rmsnorm.forward followed by forward_down)
 // Kernels and C ABI in libqwen_b200.so (include/qwen_b200_ops.h).  fp16 only;
 // `backward` (training) is not part of this build and raises.
+// forward_down and rmsnorm_forward_down take one keyword more, `exact`:
+//   None (default)  tensor cores (tcgen05, fp32 accumulation) from 64 rows on,
+//                   upstream's fp16 accumulation chain (bit-identical) below;
+//   True            the fp16 chain at every size (bit-identical to upstream);
+//   False           the tensor cores at every size.
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
@@ -80,8 +85,11 @@ std::vector<torch::Tensor> forward(torch::Tensor x, torch::Tensor w_gate, torch:
   return {out, gc, uc};
 }
 
+int mode_of(std::optional<bool> exact) { return !exact.has_value() ? -1 : (*exact ? 1 : 0); }
+
 torch::Tensor forward_down(torch::Tensor x, torch::Tensor w_gate, torch::Tensor w_up,
-                           torch::Tensor w_down, OptT b_gate, OptT b_up, OptT b_down) {
+                           torch::Tensor w_down, OptT b_gate, OptT b_up, OptT b_down,
+                           std::optional<bool> exact) {
   TORCH_CHECK(x.dim() == 3, "x must be [batch, seq, hidden], got ", x.dim(), " dimensions");
   const auto dev = x.device();
   check_half_cuda(x, "x", dev);
@@ -98,10 +106,10 @@ torch::Tensor forward_down(torch::Tensor x, torch::Tensor w_gate, torch::Tensor 
   auto out = torch::empty({B, S, H}, x.options());
   auto ws = torch::empty({qwen_b200_swiglu_forward_down_workspace(B * S, static_cast<int>(I))},
                          x.options().dtype(torch::kByte));
-  raise_if(qwen_b200_swiglu_forward_down(x.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(),
-                                         w_down.data_ptr(), bg, bu, bd, out.data_ptr(),
-                                         ws.data_ptr(), B * S, static_cast<int>(H),
-                                         static_cast<int>(I), stream_of(x)),
+  raise_if(qwen_b200_swiglu_forward_down_ex(x.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(),
+                                            w_down.data_ptr(), bg, bu, bd, out.data_ptr(),
+                                            ws.data_ptr(), B * S, static_cast<int>(H),
+                                            static_cast<int>(I), mode_of(exact), stream_of(x)),
            "swiglu_fused.forward_down");
   return out;
 }
@@ -110,7 +118,7 @@ std::vector<torch::Tensor> rmsnorm_forward_down(torch::Tensor x, torch::Tensor n
                                                 double eps, torch::Tensor w_gate,
                                                 torch::Tensor w_up, torch::Tensor w_down,
                                                 OptT residual, OptT b_gate, OptT b_up,
-                                                OptT b_down) {
+                                                OptT b_down, std::optional<bool> exact) {
   const auto dev = x.device();
   check_half_cuda(x, "x", dev);
   TORCH_CHECK(x.dim() >= 1 && x.size(-1) > 0, "x must have a non-empty last dimension");
@@ -138,11 +146,11 @@ std::vector<torch::Tensor> rmsnorm_forward_down(torch::Tensor x, torch::Tensor n
   auto ws = torch::empty(
       {qwen_b200_rmsnorm_swiglu_down_workspace(rows, static_cast<int>(H), static_cast<int>(I))},
       x.options().dtype(torch::kByte));
-  raise_if(qwen_b200_rmsnorm_swiglu_down(
+  raise_if(qwen_b200_rmsnorm_swiglu_down_ex(
                x.data_ptr(), norm_weight.data_ptr(), res, static_cast<float>(eps),
                w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), bg, bu, bd,
                normed.data_ptr(), rms.data_ptr<float>(), out.data_ptr(), ws.data_ptr(), rows,
-               static_cast<int>(H), static_cast<int>(I), stream_of(x)),
+               static_cast<int>(H), static_cast<int>(I), mode_of(exact), stream_of(x)),
            "swiglu_fused.rmsnorm_forward_down");
   return {out, normed, rms};
 }
@@ -155,12 +163,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_down", &forward_down, "Fused SwiGLU + down projection forward (B200)",
         py::arg("x"), py::arg("w_gate"), py::arg("w_up"), py::arg("w_down"),
         py::arg("b_gate") = py::none(), py::arg("b_up") = py::none(),
-        py::arg("b_down") = py::none());
+        py::arg("b_down") = py::none(), py::arg("exact") = py::none());
   m.def("rmsnorm_forward_down", &rmsnorm_forward_down,
         "RMSNorm followed by SwiGLU + down projection (B200)", py::arg("x"),
         py::arg("norm_weight"), py::arg("eps"), py::arg("w_gate"), py::arg("w_up"),
         py::arg("w_down"), py::arg("residual") = py::none(), py::arg("b_gate") = py::none(),
-        py::arg("b_up") = py::none(), py::arg("b_down") = py::none());
+        py::arg("b_up") = py::none(), py::arg("b_down") = py::none(),
+        py::arg("exact") = py::none());
   m.def(
       "backward",
       [](py::args, py::kwargs) {

@@ -182,3 +182,59 @@ def test_gemm_rejects_bad_shapes():
     rc = f(EPI_F16, a.data_ptr(), a.data_ptr(), a.data_ptr(), None, None, 4, 4, 100, 4, 1, None)
     code, msg = last_error()
     assert rc != 0 and rc == code and "multiple" in msg
+
+
+def gemm_tiled(epi, a, b, bn, res=None, k_splits=1, workspace=True):
+    f = lib().qwen_b200_gemm_f16_tiled
+    vp, i = ctypes.c_void_p, ctypes.c_int
+    f.restype = i
+    f.argtypes = [i, vp, vp, vp, vp, vp, i, i, i, i, i, i, vp]
+    M, K = a.shape
+    N = b.shape[0]
+    if epi == EPI_SWIGLU:
+        out = torch.empty(M, N // 2, dtype=torch.float16, device="cuda")
+    elif epi in (EPI_F32, EPI_F32_RES16):
+        out = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    else:
+        out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ws = torch.empty(max(16, k_splits * M * N * 4), dtype=torch.uint8, device="cuda") if workspace else None
+    rc = f(epi, a.data_ptr(), b.data_ptr(), out.data_ptr(), res.data_ptr() if res is not None else None,
+           ws.data_ptr() if ws is not None else None, M, N, K, N, k_splits, bn,
+           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc:
+        raise RuntimeError(last_error())
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("M,N,K", [(256, 4096, 1024), (130, 1024, 3072), (7, 256, 128)])
+def test_gemm_tile_widths(bn, M, N, K):
+    """Every tile width gives the reference result (256 columns: one
+    128 x 256 accumulator per CTA, 48 KB ring stages)."""
+    a, b = _inputs(M, N, K, bn + M)
+    ref = ref_mm(a, b)
+    _close16(gemm_tiled(EPI_F16, a, b, bn), ref, f"bn {bn}")
+    r32 = torch.randn(M, N, device="cuda")
+    _close16(gemm_tiled(EPI_F16_RES32, a, b, bn, res=r32, k_splits=4), ref + r32, f"bn {bn} split")
+    _close16(gemm_tiled(EPI_F16, a, b, bn, k_splits=4, workspace=False), ref, f"bn {bn} cluster split")
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_swiglu_after_split_k(bn):
+    """The SwiGLU epilogue after a split-K reduction (cluster and partials
+    forms give the same bits as each other and as the unsplit GEMM, up to the
+    fp32 summation order of the slices)."""
+    M, N, K = 256, 6144, 1024
+    a, b = _inputs(M, N, K, 31)
+    one = gemm_tiled(EPI_SWIGLU, a, b, bn)
+    cl = gemm_tiled(EPI_SWIGLU, a, b, bn, k_splits=2, workspace=False)
+    part = gemm_tiled(EPI_SWIGLU, a, b, bn, k_splits=2)
+    assert torch.equal(cl, part)
+    ref = ref_mm(a, b)
+    gate, up = ref[:, 0::2], ref[:, 1::2]
+    want = (silu_half_ref(gate.half()).float() * up).half()
+    for out in (one, cl):
+        err = (out.float() - want.float()).abs()
+        tol = 2 * want.float().abs().clamp_min(6e-5) * 2.0 ** -10 + 2e-3 * up.abs() + 1e-3
+        assert not bool((err > tol).any()), float(err.max())

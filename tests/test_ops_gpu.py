@@ -107,7 +107,7 @@ def test_swiglu_large_batch(b):
     rf, rgc, ruc = O.swiglu_forward(xs, wg, wu)
     assert torch.equal(gc.cpu(), rgc) and torch.equal(uc.cpu(), ruc)
     assert max_ulps(f, rf) <= 1 and float((f.cpu() == rf).float().mean()) >= 0.999
-    y = sw.forward_down(xs.cuda(), wg.cuda(), wu.cuda(), wd.cuda())
+    y = sw.forward_down(xs.cuda(), wg.cuda(), wu.cuda(), wd.cuda(), exact=True)
     assert torch.equal(y.cpu().view(b, 1024), down_chain(f.view(b, 3072), wd))
 
 
@@ -189,3 +189,92 @@ def test_operator_errors_and_empty_inputs():
     st = ctypes.c_uint64(0)
     lib().qwen_b200_ops_status.restype = ctypes.c_int
     assert lib().qwen_b200_ops_status(ctypes.byref(st)) == 0
+
+
+# ---------------------------------------------------------------- tensor cores
+# forward_down / rmsnorm_forward_down with exact=False (and by default from 64
+# rows): tcgen05 GEMMs with fp32 accumulation instead of upstream's fp16
+# chains.  Acceptance: every output at least as close to a float64 evaluation
+# of the same operator (SwiGLU activations rounded to fp16 only where the
+# operator itself stores them: not at all in the reference) as upstream's
+# output, plus one fp16 ulp of the reference value.
+
+def _ref64(x, wg, wu, wd, bg=None, bu=None, bd=None):
+    x = x.double().reshape(-1, x.shape[-1])
+    g = x @ wg.double()
+    u = x @ wu.double()
+    if bg is not None:
+        g = g + bg.double()
+    if bu is not None:
+        u = u + bu.double()
+    s = g / (1.0 + torch.exp(-g)) * u
+    y = s @ wd.double()
+    if bd is not None:
+        y = y + bd.double()
+    return y
+
+
+def _ulp(ref: torch.Tensor) -> torch.Tensor:
+    """fp16 ulp at |ref|: 2^(e - 11) for |ref| = m 2^e, m in [0.5, 1); 2^-24 at the bottom."""
+    _, e = torch.frexp(ref.abs())
+    return torch.pow(2.0, (e - 11).to(torch.float64)).clamp_min(2.0 ** -24)
+
+
+def _check_closer(tc, chain, ref, what):
+    tc, chain = tc.cpu().double().reshape(ref.shape), chain.cpu().double().reshape(ref.shape)
+    e_tc, e_up = (tc - ref).abs(), (chain - ref).abs()
+    bad = e_tc > e_up + _ulp(ref)
+    assert not bool(bad.any()), (f"{what}: {int(bad.sum())} of {bad.numel()} outputs farther from the "
+                                 f"float64 value than upstream's + 1 ulp; worst excess "
+                                 f"{float((e_tc - e_up - _ulp(ref)).max()):.3g}")
+    return float(e_tc.max()), float(e_up.max())
+
+
+@pytest.mark.parametrize("b", [64, 256, 1, 8, 129])
+def test_swiglu_forward_down_tensor_cores(b):
+    _, sw = _mods()
+    x, w, _, wg, wu, wd = ops_inputs(b)
+    xg = x.cuda().view(b, 1, 1024)
+    wgc, wuc, wdc = wg.cuda(), wu.cuda(), wd.cuda()
+    tc = sw.forward_down(xg, wgc, wuc, wdc, exact=False)
+    chain = sw.forward_down(xg, wgc, wuc, wdc, exact=True)
+    ref = _ref64(x, wg, wu, wd)
+    e_tc, e_up = _check_closer(tc, chain, ref, f"B={b}")
+    assert e_tc < e_up, (e_tc, e_up)
+    if b >= 64:  # the default takes the tensor cores from 64 rows on
+        assert torch.equal(sw.forward_down(xg, wgc, wuc, wdc), tc)
+    else:
+        assert torch.equal(sw.forward_down(xg, wgc, wuc, wdc), chain)
+
+
+def test_swiglu_forward_down_tensor_cores_biases():
+    _, sw = _mods()
+    b = 96
+    x, w, _, wg, wu, wd = ops_inputs(b)
+    g = torch.Generator().manual_seed(11)
+    bg, bu = (0.1 * torch.randn(3072, generator=g)).half(), (0.1 * torch.randn(3072, generator=g)).half()
+    bd = (0.1 * torch.randn(1024, generator=g)).half()
+    args = [t.cuda() for t in (wg, wu, wd, bg, bu, bd)]
+    xg = x.cuda().view(b, 1, 1024)
+    tc = sw.forward_down(xg, *args, exact=False)
+    chain = sw.forward_down(xg, *args, exact=True)
+    _check_closer(tc, chain, _ref64(x, wg, wu, wd, bg, bu, bd), "biases")
+
+
+@pytest.mark.parametrize("b", [64, 256])
+def test_rmsnorm_forward_down_tensor_cores(b):
+    rn, sw = _mods()
+    x, w, resid, wg, wu, wd = ops_inputs(b)
+    args = [t.cuda() for t in (wg, wu, wd)]
+    out_tc, normed_tc, rms_tc = sw.rmsnorm_forward_down(x.cuda(), w.cuda(), OPS_CASE["eps"], *args,
+                                                        exact=False)
+    out_ch, normed_ch, rms_ch = sw.rmsnorm_forward_down(x.cuda(), w.cuda(), OPS_CASE["eps"], *args,
+                                                        exact=True)
+    # The RMSNorm half is the same kernel either way.
+    assert torch.equal(normed_tc, normed_ch) and torch.equal(rms_tc, rms_ch)
+    _check_closer(out_tc, out_ch, _ref64(normed_ch.cpu(), wg, wu, wd), f"rmsnorm B={b}")
+    # Against upstream's own operators where the golden file holds them.
+    g = _golden()
+    if f"swd_out_{b}" in g.files:
+        up = _h(g[f"swd_out_{b}"]).view(b, 1024)
+        assert float((out_tc.cpu().float() - up.float()).abs().max()) < 5e-2
