@@ -624,17 +624,26 @@ def run_sample(args, world: int, rank: int, local: int, dev, dist) -> None:
 
 
 def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
+    line = lmhead_line(args, world, rank, local, dev, dist, args.batch)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def lmhead_line(args, world: int, rank: int, local: int, dev, dist, B: int, with_cpu: bool = True) -> dict:
     """Config 5: tied lm_head + greedy argmax with the vocabulary split over the
-    ranks (one contiguous row block each), the (max, index) pairs all-gathered
-    over NCCL.  One step = the argmax of `batch` hidden rows over the whole
-    vocabulary; total work is fixed, so scaling is strong."""
+    ranks (one contiguous row block each), the per-row (max, index) pairs
+    exchanged through peer memory (one kernel per rank, default) or an NCCL
+    all-gather (--exchange nccl).  One step = the argmax of B hidden rows over
+    the whole vocabulary; total work is fixed, so scaling is strong."""
     from lmhead_shard import HIDDEN, VOCAB, ShardedLMHead
 
-    B = args.batch
     g = torch.Generator(device=dev).manual_seed(SEED)
     emb = (0.02 * torch.randn(VOCAB, HIDDEN, generator=g, device=dev)).half()
     x = torch.randn(B, HIDDEN, generator=g, device=dev).half()
-    head = ShardedLMHead(emb, world, rank, device=dev, max_rows=B)
+    head = ShardedLMHead(emb, world, rank, device=dev, max_rows=B, exchange=args.exchange)
     del emb
     torch.cuda.empty_cache()
     stream = torch.cuda.current_stream(dev)
@@ -693,7 +702,9 @@ def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
         "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,0.02) embedding, N(0,1) hidden rows)",
         "config": {"workload": f"config 5: tied lm_head + greedy argmax of {B} hidden rows, vocabulary "
-                               f"split over {world} GPU(s), (max, index) pairs all-gathered over NCCL",
+                               f"split over {world} GPU(s), (max, index) pairs "
+                               + ("stored into every rank's buffer through peer memory (one kernel)"
+                                  if head.exchange == "peer" else "all-gathered over NCCL"),
                    "batch": B, "parallelism": f"vocab shards x{world}" if world > 1 else "single GPU",
                    "l2": f"weights of a shard ({(head.hi - head.lo) * HIDDEN * 2 / 1e6:.1f} MB) are re-read "
                          "each step; no flush" + (" (a shard fits in L2 at 8 GPUs)" if world >= 4 else "")},
@@ -702,10 +713,13 @@ def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
                      "algorithmic_bytes_per_step": shard_bytes, "avg_step_ms": avg_step_s * 1000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": B * HIDDEN * 2,
                 "d2h_bytes_per_step": 4 * B},
-        "gpu_launches": args.steps * 3,
+        "gpu_launches": args.steps * (2 if (world == 1 or head.exchange == "peer") else 3),
         "clocks": clk,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if head.exchange == "peer" and head.device_status() != 0:
+        raise RuntimeError(f"peer exchange wait gave up: status {head.device_status():#x}")
+    head.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and with_cpu:
         threads = len(os.sched_getaffinity(0))
         torch.set_num_threads(threads)
         e_cpu = (0.02 * torch.randn(VOCAB, HIDDEN, generator=torch.Generator().manual_seed(2))).float()
@@ -718,11 +732,7 @@ def run_lmhead(args, world: int, rank: int, local: int, dev, dist) -> None:
         line["cpu_baseline"] = {"value": B * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
                                 "sample": f"{n} fp32 torch matmul + argmax of {B} rows over the full "
                                           f"vocabulary on the host ({dt:.1f} s)"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
 
 
 def main() -> None:
@@ -751,6 +761,8 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--seqs", type=int, default=256, help="sequences per GPU (batched workload)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="lmhead workload: how the ranks exchange their (max, index) pairs")
     ap.add_argument("--exact", action="store_true",
                     help="ops workload: upstream's fp16 accumulation chains (bit-exact) at every batch size")
     args = ap.parse_args()
@@ -906,6 +918,11 @@ def main() -> None:
         keep = ("value", "unit", "ms_per_step", "steps", "warmup", "scaling", "config", "roofline",
                 "e2e", "gpu_launches", "clocks", "cpu_baseline")
         line["batched"] = {k: b[k] for k in keep if k in b}
+        torch.cuda.empty_cache()
+        # Config 5 (vocabulary-sharded lm_head, B = 256) at the same N.
+        lm = lmhead_line(args, world, rank, local, dev, dist, 256, with_cpu=False)
+        line["lmhead"] = {k: lm[k] for k in ("value", "unit", "ms_per_step", "steps", "scaling", "config",
+                                             "roofline", "e2e", "gpu_launches", "clocks") if k in lm}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -60,6 +60,36 @@ long long qwen_b200_gemm_argmax_workspace(int M, int N);
  * qwen_b200_argmax_pick: vals / idxs [world, rows] (every shard's pair, e.g.
  * after an all-gather) -> out[r], the largest value's index, lowest on ties.
  */
+/*
+ * Exchange of the shards' (max, index) pairs through peer memory instead of
+ * an all-gather (no upstream counterpart).  Every rank owns a receive buffer
+ * of qwen_b200_peer_buffer_bytes(world, rows) bytes made by
+ * qwen_b200_peer_buffer_create (cudaMalloc'd, cleared, with its 64-byte CUDA
+ * IPC handle written to ipc_handle); ranks share the handles (e.g. through
+ * torch.distributed) and open each other's buffers with
+ * qwen_b200_peer_buffer_open (a pointer valid on this device, peer access
+ * enabled lazily); qwen_b200_peer_buffer_close releases an opened buffer
+ * (opened = 1) or frees an own one (opened = 0) -- close the peers' mappings
+ * of a buffer before it is freed.
+ * qwen_b200_argmax_exchange: rank `rank` stores its pair of each row, tagged
+ * with `epoch`, into every rank's buffer (peer_bufs[q]: rank q's buffer as
+ * seen from this device, peer_bufs[rank] its own) with plain 8-byte stores at
+ * system scope, then waits until every rank's pairs of this epoch are in its
+ * own buffer and writes out[r] = the largest value's index (lowest among equal
+ * values).  epoch: nonzero, one more per call, the same on every rank;
+ * consecutive calls use the two halves of the buffers in turn.  Each wait is
+ * bounded by timeout_ns (<= 0: 2 s): a rank whose pairs never come gives -1
+ * and, when status is not NULL, (1 << 32 | rank << 24 | row) in *status.
+ * world <= 8.
+ */
+long long qwen_b200_peer_buffer_bytes(int world, int rows);
+int qwen_b200_peer_buffer_create(long long bytes, void **ptr, void *ipc_handle);
+int qwen_b200_peer_buffer_open(const void *ipc_handle, void **ptr);
+int qwen_b200_peer_buffer_close(void *ptr, int opened);
+int qwen_b200_argmax_exchange(const float *val, const int *idx, void *const *peer_bufs, int world,
+                              int rank, int rows, unsigned epoch, long long timeout_ns, int *out,
+                              unsigned long long *status, void *stream);
+
 long long qwen_b200_lmhead_argmax_workspace(int rows, int vocab_rows);
 int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, int vocab_rows,
                             long long index_offset, float *out_val, int *out_idx, void *workspace,

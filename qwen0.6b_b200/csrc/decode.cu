@@ -11,7 +11,7 @@
 //    evict-first).  Weights do not depend on activations, so the producer runs
 //    ahead across stage boundaries, layers and decode steps; HBM keeps
 //    streaming while the consumer warps wait for the previous stage.
-//  * 16 consumer warps compute each stage on the bytes already in shared
+//  * 8 consumer warps compute each stage on the bytes already in shared
 //    memory.  Per layer: A input RMSNorm + QKV GEMV, B q/k RMSNorm + RoPE +
 //    split-KV GQA attention (2 q heads share one K/V read), C o_proj +
 //    residual, D post-attention RMSNorm + gate/up GEMV + SiLU*mul, E down GEMV

@@ -410,32 +410,43 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int nvalid = min(16, nout - col);
         const size_t o = static_cast<size_t>(row) * g.ldo + col;
         __half *out = static_cast<__half *>(g.out) + o;
-        __align__(16) __half hv[16], lv[16], gh[16], uh[16];
+        // Eight packed pairs per output (s hi, s lo, gate, up), stored as two
+        // 16-byte stores each when the 16 columns are whole and aligned (the
+        // planned shapes), else element by element.
+        uint32_t ph[8], pl[8], pg[8], pu[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const bool in = i < nvalid;
-          const float gg = (g.bias != nullptr && in) ? __fadd_rn(gv[i], __half2float(static_cast<const __half *>(g.bias)[col + i])) : gv[i];
-          const float uu = (g.bias2 != nullptr && in) ? __fadd_rn(uv[i], __half2float(static_cast<const __half *>(g.bias2)[col + i])) : uv[i];
-          const float sv = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
-          hv[i] = __float2half_rn(sv);
-          lv[i] = __float2half_rn(__fsub_rn(sv, __half2float(hv[i])));
-          gh[i] = __float2half_rn(gg);
-          uh[i] = __float2half_rn(uu);
+        for (int i = 0; i < 16; i += 2) {
+          float sv[2], gg[2], uu[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const bool in = i + j < nvalid;
+            gg[j] = (g.bias != nullptr && in) ? __fadd_rn(gv[i + j], __half2float(static_cast<const __half *>(g.bias)[col + i + j])) : gv[i + j];
+            uu[j] = (g.bias2 != nullptr && in) ? __fadd_rn(uv[i + j], __half2float(static_cast<const __half *>(g.bias2)[col + i + j])) : uv[i + j];
+            sv[j] = __fmul_rn(__fdiv_rn(gg[j], __fadd_rn(1.0f, expf(-gg[j]))), uu[j]);
+          }
+          const __half2 hi = __floats2half2_rn(sv[0], sv[1]);
+          const __half2 lo = __floats2half2_rn(__fsub_rn(sv[0], __low2float(hi)), __fsub_rn(sv[1], __high2float(hi)));
+          const __half2 gh = __floats2half2_rn(gg[0], gg[1]);
+          const __half2 uh = __floats2half2_rn(uu[0], uu[1]);
+          ph[i / 2] = *reinterpret_cast<const uint32_t *>(&hi);
+          pl[i / 2] = *reinterpret_cast<const uint32_t *>(&lo);
+          pg[i / 2] = *reinterpret_cast<const uint32_t *>(&gh);
+          pu[i / 2] = *reinterpret_cast<const uint32_t *>(&uh);
         }
-        // 16-byte stores when the 16 columns are whole (ldo, lo_col and col
-        // are multiples of 8 on the planned shapes), else element by element.
-        auto put = [&](__half *dst, const __half (&src)[16]) {
+        auto put = [&](__half *dst, const uint32_t (&p)[8]) {
           if (nvalid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-            reinterpret_cast<uint4 *>(dst)[0] = reinterpret_cast<const uint4 *>(src)[0];
-            reinterpret_cast<uint4 *>(dst)[1] = reinterpret_cast<const uint4 *>(src)[1];
+            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(p[0], p[1], p[2], p[3]);
+            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
           } else {
-            for (int i = 0; i < nvalid; ++i) dst[i] = src[i];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i < nvalid) dst[i] = __ushort_as_half(static_cast<unsigned short>(p[i / 2] >> (16 * (i & 1))));
           }
         };
-        put(out, hv);
-        if (g.lo_col > 0) put(out + g.lo_col, lv);
-        if (g.out2 != nullptr) put(static_cast<__half *>(g.out2) + o, gh);
-        if (g.out3 != nullptr) put(static_cast<__half *>(g.out3) + o, uh);
+        put(out, ph);
+        if (g.lo_col > 0) put(out + g.lo_col, pl);
+        if (g.out2 != nullptr) put(static_cast<__half *>(g.out2) + o, pg);
+        if (g.out3 != nullptr) put(static_cast<__half *>(g.out3) + o, pu);
       }
     } else if (ok) {
       const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
