@@ -191,6 +191,8 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mb
   GemmArgs ga = g;
   const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
   ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
+  // The epilogue stages its tiles in the ring.
+  ga.stages = max(ga.stages, GemmSmem<BN>::min_stages(ga.cluster_k != 0 && grid.z > 1));
   const cudaError_t e = qb200_launch_cl(gemm_tc_kernel<BN, EPI, BL>, grid, dim3(THREADS),
                                         GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0,
                                         ga.cluster_k ? static_cast<int>(grid.z) : 1, ma, mb, mb2, ga);

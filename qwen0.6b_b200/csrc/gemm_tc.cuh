@@ -44,6 +44,10 @@ constexpr int max_stages() {
   return BN == 64 ? 8 : (BN == 128 ? 6 : 4);  // 24 / 32 / 48 KB stages
 }
 constexpr int THREADS = 192;           // 6 warps
+// Row pitch (floats) of an epilogue warp's staging tile: 32 rows of up to 96
+// values; 25 16-byte units per row (odd), so the row-parallel writes of 32
+// lanes and the row-contiguous reads both spread over all banks.
+constexpr int EPI_PITCH = 100;
 constexpr long long WAIT_NS = 2000000000LL;
 
 enum Epilogue : int {
@@ -97,6 +101,13 @@ struct GemmSmem {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr size_t bytes(int stages) { return static_cast<size_t>(stages) * STAGE + 256 + 1024; }
+  // Ring stages the epilogue needs for its staging tiles: the clustered
+  // split-K partial tile (128 rows of BN + 4 floats) or four warps' staging
+  // rows (32 x EPI_PITCH floats each).
+  static constexpr int min_stages(bool clustered) {
+    const int need = clustered ? BM * (BN + 4) * 4 : 4 * 32 * EPI_PITCH * 4;
+    return (need + STAGE - 1) / STAGE;
+  }
 };
 
 // ------------------------------------------------------------------ PTX
@@ -141,13 +152,24 @@ __device__ __forceinline__ constexpr uint32_t idesc_f16(bool b_mn = false) {
          (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t idesc, uint32_t accumulate) {
+// One k-block (K = 4 x 16) on a converged warp: an elected lane issues the
+// four MMAs and the commit of their completion to the mbarrier at `bar`
+// (shared address); the first MMA accumulates when `acc` is non-zero.
+static_assert(BK == 64, "mma4_commit_elect covers one 64-element k-block");
+__device__ __forceinline__ void mma4_commit_elect(uint32_t tmem_d, uint64_t a0, uint64_t a1, uint64_t a2,
+                                                  uint64_t a3, uint64_t b0, uint64_t b1, uint64_t b2,
+                                                  uint64_t b3, uint32_t idesc, uint32_t acc, uint32_t bar) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "{\n\t.reg .pred p, q, t;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %10, 0;\n\t"
+      "setp.eq.b32 t, 0, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, q;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, t;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, t;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, t;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t}" ::"r"(tmem_d),
+      "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc), "r"(bar)
       : "memory");
 }
 
@@ -177,19 +199,31 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-// 16 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// Two 32-column TMEM loads of this thread's lane (at taddr0 and taddr1) and
+// one wait: v[0..31] from taddr0, v[32..63] from taddr1.  Loads and wait
+// are one asm statement, so no use of v can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr0, uint32_t taddr1, float (&v)[64]) {
+  uint32_t r[64];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr0), "r"(taddr1)
+      : "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -255,6 +289,211 @@ __device__ __forceinline__ __half silu_half(__half x) {
   return __hmul_rn(x, r);
 }
 
+// Output dtype of a staged epilogue.
+template <int EPI>
+constexpr bool kEpiF16Out = EPI == EPI_F16 || EPI == EPI_F16_RES32 || EPI == EPI_SWIGLU;
+
+// Eight consecutive outputs x[0..7] of one row at element offset o: the
+// epilogue's last step (residual, rounding) and the store, as two or one
+// 16-byte accesses when `vec`, else element by element.
+template <int EPI>
+__device__ __forceinline__ void store_unit8(const GemmArgs &g, size_t o, float (&x)[8], bool vec) {
+  if constexpr (EPI == EPI_F32_RES16) {
+    const __half *r = static_cast<const __half *>(g.res) + o;
+    if (vec) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(r);
+      const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __fadd_rn(x[2 * i], __low2float(h[i]));
+        x[2 * i + 1] = __fadd_rn(x[2 * i + 1], __high2float(h[i]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __fadd_rn(x[i], __half2float(r[i]));
+    }
+  } else if constexpr (EPI == EPI_F16_RES32) {
+    const float *r = static_cast<const float *>(g.res) + o;
+    if (vec) {
+      const float4 a = reinterpret_cast<const float4 *>(r)[0], b = reinterpret_cast<const float4 *>(r)[1];
+      const float rr[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __fadd_rn(x[i], rr[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __fadd_rn(x[i], r[i]);
+    }
+  }
+  if constexpr (kEpiF16Out<EPI>) {
+    __half *out = static_cast<__half *>(g.out) + o;
+    if (vec) {
+      uint4 pk;
+      __half2 *h = reinterpret_cast<__half2 *>(&pk);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+      *reinterpret_cast<uint4 *>(out) = pk;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out[i] = __float2half_rn(x[i]);
+    }
+  } else {
+    float *out = static_cast<float *>(g.out) + o;
+    if constexpr (EPI == EPI_PARTIAL) out += static_cast<size_t>(blockIdx.z) * g.M * g.ldo;
+    if (vec) {
+      reinterpret_cast<float4 *>(out)[0] = make_float4(x[0], x[1], x[2], x[3]);
+      reinterpret_cast<float4 *>(out)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out[i] = x[i];
+    }
+  }
+}
+
+// Epilogue of one warp (rows rbase..rbase+31 of the tile, TMEM lanes at tq)
+// for EPI_F16, EPI_F32, EPI_F32_RES16, EPI_F16_RES32, EPI_SWIGLU and
+// EPI_PARTIAL.  Per 64 accumulator columns: one TMEM load per row (thread),
+// the per-element math of the epilogue, the fp32 results into the warp's
+// staging rows; then the warp stores the 32 rows row-contiguously, 8 outputs
+// per lane and step (the residual is added there), so that each store
+// instruction writes whole 128-byte lines instead of 32 scattered pieces.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_staged(const GemmArgs &g, uint32_t tq, float *stg, int rbase, int n0,
+                                                int lane) {
+  constexpr bool PAIRS = EPI == EPI_SWIGLU;  // (gate, up) column pairs -> one output
+  constexpr int OUTS = PAIRS ? 32 : 64;      // outputs per 64 accumulator columns
+  constexpr int UPR = OUTS / 8;              // 8-output units per row
+  const int nout = PAIRS ? g.N / 2 : g.N;
+  const size_t esz = kEpiF16Out<EPI> ? 2 : 4;
+  bool vec = (reinterpret_cast<uintptr_t>(g.out) & 15u) == 0 && (static_cast<size_t>(g.ldo) * esz) % 16 == 0;
+  if constexpr (EPI == EPI_F32_RES16 || EPI == EPI_F16_RES32)
+    vec = vec && (reinterpret_cast<uintptr_t>(g.res) & 15u) == 0 && (g.ldo % 8) == 0;
+  float *srow = stg + lane * EPI_PITCH;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 64) {
+    const int oc0 = PAIRS ? (n0 + c0) / 2 : n0 + c0;
+    if (oc0 >= nout) break;  // warp-uniform
+    float v[64];
+    tmem_ld64(tq + c0, tq + c0 + 32, v);
+    if constexpr (PAIRS) {
+      // out = half(float(silu_half(half(gate))) * up), kept exactly as fp32.
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = __half2float(__float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(v[2 * i]))), v[2 * i + 1])));
+    } else if constexpr (EPI == EPI_F16) {
+      if (g.bias != nullptr) {
+        const __half *b = static_cast<const __half *>(g.bias) + oc0;
+        const int nv = min(64, nout - oc0);
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < nv) v[i] = __fadd_rn(v[i], __half2float(b[i]));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < OUTS / 4; ++i)
+      reinterpret_cast<float4 *>(srow)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    __syncwarp();
+#pragma unroll 1
+    for (int u = lane; u < 32 * UPR; u += 32) {
+      const int r = u / UPR, j = u % UPR;
+      const int row = rbase + r, oc = oc0 + 8 * j;
+      if (row >= g.M || oc >= nout) continue;
+      const float4 *s4 = reinterpret_cast<const float4 *>(stg + r * EPI_PITCH) + 2 * j;
+      const float4 a = s4[0], b = s4[1];
+      float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      store_unit8<EPI>(g, static_cast<size_t>(row) * g.ldo + oc, x, vec);
+    }
+    __syncwarp();  // the staging rows are rewritten by the next chunk
+  }
+}
+
+// Eight halves into dst: one 16-byte store when `vec`, else element by element.
+__device__ __forceinline__ void put_half8(__half *dst, const float (&x)[8], bool vec) {
+  if (vec) {
+    uint4 pk;
+    __half2 *h = reinterpret_cast<__half2 *>(&pk);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(dst) = pk;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[i] = __float2half_rn(x[i]);
+  }
+}
+
+// EPI_SWIGLU2 epilogue of one warp: accumulator columns [0, BN/2) are the
+// gate and [BN/2, BN) the up projections of output columns n0/2 + c.  Per 32
+// outputs: g and u (bias added in fp32), s = g / (1 + exp(-g)) * u staged as
+// fp32, then stored row-contiguously as half(s), the residual
+// half(s - half(s)) at column lo_col + c, and the gate / up caches.
+template <int BN>
+__device__ __forceinline__ void epilogue_swiglu2(const GemmArgs &g, uint32_t tq, float *stg, int rbase, int n0,
+                                                 int lane) {
+  const int nout = g.N / 2;
+  __half *out = static_cast<__half *>(g.out);
+  __half *out2 = static_cast<__half *>(g.out2);
+  __half *out3 = static_cast<__half *>(g.out3);
+  const __half *bias = static_cast<const __half *>(g.bias);
+  const __half *bias2 = static_cast<const __half *>(g.bias2);
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec = al(out) && (g.ldo % 8) == 0 && (g.lo_col % 8) == 0 && (out2 == nullptr || al(out2)) &&
+                   (out3 == nullptr || al(out3));
+  float *srow = stg + lane * EPI_PITCH;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+    const int oc0 = n0 / 2 + c0;
+    if (oc0 >= nout) break;  // warp-uniform
+    float v[64];
+    tmem_ld64(tq + c0, tq + BN / 2 + c0, v);
+    const int nv = min(32, nout - oc0);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float gg = (bias != nullptr && i < nv) ? __fadd_rn(v[i], __half2float(bias[oc0 + i])) : v[i];
+      const float uu = (bias2 != nullptr && i < nv) ? __fadd_rn(v[32 + i], __half2float(bias2[oc0 + i])) : v[32 + i];
+      v[i] = gg;
+      v[32 + i] = uu;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      reinterpret_cast<float4 *>(srow + 32)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      reinterpret_cast<float4 *>(srow + 64)[i] =
+          make_float4(v[32 + 4 * i], v[33 + 4 * i], v[34 + 4 * i], v[35 + 4 * i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), v[32 + i]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      reinterpret_cast<float4 *>(srow)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    __syncwarp();
+#pragma unroll 1
+    for (int u = lane; u < 32 * 4; u += 32) {
+      const int r = u >> 2, j = u & 3;
+      const int row = rbase + r, oc = oc0 + 8 * j;
+      if (row >= g.M || oc >= nout) continue;
+      const float *sr = stg + r * EPI_PITCH + 8 * j;
+      float s[8], lo[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        s[i] = sr[i];
+        lo[i] = __fsub_rn(s[i], __half2float(__float2half_rn(s[i])));
+      }
+      const size_t o = static_cast<size_t>(row) * g.ldo + oc;
+      put_half8(out + o, s, vec);
+      if (g.lo_col > 0) put_half8(out + o + g.lo_col, lo, vec);
+      if (out2 != nullptr || out3 != nullptr) {
+        float gg[8], uu[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          gg[i] = sr[32 + i];
+          uu[i] = sr[64 + i];
+        }
+        if (out2 != nullptr) put_half8(out2 + o, gg, vec);
+        if (out3 != nullptr) put_half8(out3 + o, uu, vec);
+      }
+    }
+    __syncwarp();  // the staging rows are rewritten by the next chunk
+  }
+}
+
 template <int BN, int EPI, int BL = BL_K>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -317,12 +556,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   // grid before it reads anything this grid writes.
   if (threadIdx.x == 0) qb200::griddep_launch_dependents();
 
+  // The producer and MMA warps run their loops as whole warps (every lane
+  // waits on the barriers) and one lane issues; the MMAs go out predicated
+  // on an elected lane, which keeps the warp converged around them (a branch
+  // to a single lane around each k-block's MMAs costs ~60 % more issue time).
   if (warp == 0) {
+    // B (weights) does not depend on the preceding kernel: the first ring
+    // stages are armed and their weight tiles requested before the grid
+    // dependency wait; A (activations) follows it.
+    const int pre = min(STAGES, nk);
     if (lane == 0) {
-      // B (weights) does not depend on the preceding kernel: the first ring
-      // stages are armed and their weight tiles requested before the grid
-      // dependency wait; A (activations) follows it.
-      const int pre = min(STAGES, nk);
       for (int kb = 0; kb < pre; ++kb) {
         uint8_t *st = base + kb * S::STAGE;
         mbar_arrive_expect_tx(&full[kb], S::STAGE);
@@ -331,201 +574,107 @@ __global__ void __launch_bounds__(THREADS, 1)
       qb200::griddep_wait();
       for (int kb = 0; kb < pre; ++kb)
         tma_load_2d(base + kb * S::STAGE, &tm_a, (kb0 + kb) * BK, m0, &full[kb]);
-      int issued = pre;
-      for (int kb = pre; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (!gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
+    }
+    __syncwarp();
+    int issued = pre;
+    for (int kb = pre; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      if (!gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
+      if (lane == 0) {
         uint8_t *st = base + s * S::STAGE;
         mbar_arrive_expect_tx(&full[s], S::STAGE);
         tma_load_2d(st, &tm_a, (kb0 + kb) * BK, m0, &full[s]);
         load_b(st + S::A_BYTES, kb0 + kb, &full[s]);
-        issued = kb + 1;
       }
-      // Every issued copy lands before the CTA may exit (matters after an abort).
-      for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1))
-          if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
-            gemm_record(g.err, 4);
-            break;
-          }
-      }
+      __syncwarp();
+      issued = kb + 1;
+    }
+    // Every issued copy lands before the CTA may exit (matters after an abort).
+    for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1))
+        if (static_cast<long long>(globaltimer_ns() - t0) > WAIT_NS) {
+          if (lane == 0) gemm_record(g.err, 4);
+          break;
+        }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16<BN>(BL != BL_K);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (!gemm_wait(&full[s], (kb / STAGES) & 1, abort, g.err, 2)) break;
-        tc_fence_after();
-        const uint32_t sa = smem_u32(base + s * S::STAGE);
-        const uint32_t sb = sa + S::A_BYTES;
+    constexpr uint32_t idesc = idesc_f16<BN>(BL != BL_K);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES;
+      if (!gemm_wait(&full[s], (kb / STAGES) & 1, abort, g.err, 2)) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(base + s * S::STAGE);
+      const uint32_t sb = sa + S::A_BYTES;
+      // K-major operands advance 16 elements (32 bytes) along their rows per
+      // MMA; an MN-major B advances 16 rows (two 1024-byte atoms).
+      uint64_t bd[4];
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          // K-major B advances 16 elements (32 bytes) along its rows; MN-major
-          // B advances 16 rows (two 1024-byte atoms).
-          const uint64_t bd = BL == BL_K ? sw128_desc(sb + 32 * k) : sw128_mn_desc(sb + 2048 * k, BK * 128);
-          mma_f16(tmem, sw128_desc(sa + 32 * k), bd, idesc, (kb | k) != 0 ? 1u : 0u);
-        }
-        mma_commit(&empty[s]);
-      }
-      // Signals the accumulator once every MMA issued above has completed
-      // (also after an abort, so tensor memory is never freed under an MMA).
-      mma_commit(acc_full);
+      for (int k = 0; k < 4; ++k) bd[k] = BL == BL_K ? sw128_desc(sb + 32 * k) : sw128_mn_desc(sb + 2048 * k, BK * 128);
+      mma4_commit_elect(tmem, sw128_desc(sa), sw128_desc(sa + 32), sw128_desc(sa + 64), sw128_desc(sa + 96), bd[0],
+                        bd[1], bd[2], bd[3], idesc, kb != 0 ? 1u : 0u, smem_u32(&empty[s]));
     }
+    // Signals the accumulator once every MMA issued above has completed
+    // (also after an abort, so tensor memory is never freed under an MMA).
+    if (lane == 0) mma_commit(acc_full);
+    __syncwarp();
   } else {
     // Epilogue warps 2..5: TMEM lane quadrant = warp % 4.  Residuals and the
     // output buffers belong to earlier kernels until the dependency wait.
     qb200::griddep_wait();
     const int q = warp & 3;
-    const int row = m0 + 32 * q + lane;
     bool ok = gemm_wait(acc_full, 0, abort, g.err, 3);
     ok = __all_sync(0xffffffffu, ok && !*abort);  // tcgen05.ld below is warp-collective
     tc_fence_after();
+    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
     if (ok && clustered) {
       // This k slice's partial tile into shared memory (the ring is idle:
       // every copy has landed and every MMA has completed).
-      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
       float *trow = reinterpret_cast<float *>(base) + (32 * q + lane) * TPITCH;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tq + c0, v);
+      for (int c0 = 0; c0 < BN; c0 += 64) {
+        float v[64];
+        tmem_ld64(tq + c0, tq + c0 + 32, v);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 16; ++i)
           reinterpret_cast<float4 *>(trow + c0)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
       }
-    } else if (ok && EPI == EPI_SWIGLU2) {
-      // Columns c of the gate half and c + BN/2 of the up half are output
-      // column n0 / 2 + c.
-      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
-      const int nout = g.N / 2;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN / 2; c0 += 16) {
-        float gv[16], uv[16];
-        tmem_ld16(tq + c0, gv);
-        tmem_ld16(tq + BN / 2 + c0, uv);
-        const int col = n0 / 2 + c0;
-        if (row >= g.M || col >= nout) continue;
-        const int nvalid = min(16, nout - col);
-        const size_t o = static_cast<size_t>(row) * g.ldo + col;
-        __half *out = static_cast<__half *>(g.out) + o;
-        // Eight packed pairs per output (s hi, s lo, gate, up), stored as two
-        // 16-byte stores each when the 16 columns are whole and aligned (the
-        // planned shapes), else element by element.
-        uint32_t ph[8], pl[8], pg[8], pu[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          float sv[2], gg[2], uu[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const bool in = i + j < nvalid;
-            gg[j] = (g.bias != nullptr && in) ? __fadd_rn(gv[i + j], __half2float(static_cast<const __half *>(g.bias)[col + i + j])) : gv[i + j];
-            uu[j] = (g.bias2 != nullptr && in) ? __fadd_rn(uv[i + j], __half2float(static_cast<const __half *>(g.bias2)[col + i + j])) : uv[i + j];
-            sv[j] = __fmul_rn(__fdiv_rn(gg[j], __fadd_rn(1.0f, expf(-gg[j]))), uu[j]);
-          }
-          const __half2 hi = __floats2half2_rn(sv[0], sv[1]);
-          const __half2 lo = __floats2half2_rn(__fsub_rn(sv[0], __low2float(hi)), __fsub_rn(sv[1], __high2float(hi)));
-          const __half2 gh = __floats2half2_rn(gg[0], gg[1]);
-          const __half2 uh = __floats2half2_rn(uu[0], uu[1]);
-          ph[i / 2] = *reinterpret_cast<const uint32_t *>(&hi);
-          pl[i / 2] = *reinterpret_cast<const uint32_t *>(&lo);
-          pg[i / 2] = *reinterpret_cast<const uint32_t *>(&gh);
-          pu[i / 2] = *reinterpret_cast<const uint32_t *>(&uh);
-        }
-        auto put = [&](__half *dst, const uint32_t (&p)[8]) {
-          if (nvalid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
-            reinterpret_cast<uint4 *>(dst)[0] = make_uint4(p[0], p[1], p[2], p[3]);
-            reinterpret_cast<uint4 *>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (i < nvalid) dst[i] = __ushort_as_half(static_cast<unsigned short>(p[i / 2] >> (16 * (i & 1))));
-          }
-        };
-        put(out, ph);
-        if (g.lo_col > 0) put(out + g.lo_col, pl);
-        if (g.out2 != nullptr) put(static_cast<__half *>(g.out2) + o, pg);
-        if (g.out3 != nullptr) put(static_cast<__half *>(g.out3) + o, pu);
-      }
-    } else if (ok) {
-      const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q) << 16);
+    } else if (ok && EPI == EPI_ARGMAX) {
+      const int row = m0 + 32 * q + lane;
       float best = -INFINITY;
       int best_i = 0x7fffffff;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tq + c0, v);
+      for (int c0 = 0; c0 < BN; c0 += 64) {
         const int col = n0 + c0;
-        if (row >= g.M || col >= g.N) continue;
-        const size_t o = static_cast<size_t>(row) * g.ldo + col;
-        const int nvalid = min(16, g.N - col);
-        if constexpr (EPI == EPI_F16) {
-          __half *out = static_cast<__half *>(g.out) + o;
-          if (g.bias != nullptr) {
-            const __half *b = static_cast<const __half *>(g.bias) + col;
-            for (int i = 0; i < nvalid; ++i) v[i] = __fadd_rn(v[i], __half2float(b[i]));
-          }
-          if (nvalid == 16) {
-            uint4 pk[2];
-            __half2 *h = reinterpret_cast<__half2 *>(pk);
+        if (col >= g.N) break;  // warp-uniform
+        float v[64];
+        tmem_ld64(tq + c0, tq + c0 + 32, v);
+        const int nvalid = min(64, g.N - col);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-            reinterpret_cast<uint4 *>(out)[0] = pk[0];
-            reinterpret_cast<uint4 *>(out)[1] = pk[1];
-          } else {
-            for (int i = 0; i < nvalid; ++i) out[i] = __float2half_rn(v[i]);
+        for (int i = 0; i < 64; ++i)
+          if (i < nvalid && v[i] > best) {
+            best = v[i];
+            best_i = col + i;
           }
-        } else if constexpr (EPI == EPI_PARTIAL) {
-          float *out = static_cast<float *>(g.out) +
-                       static_cast<size_t>(blockIdx.z) * g.M * g.ldo + o;
-          if (nvalid == 16) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              reinterpret_cast<float4 *>(out)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          } else {
-            for (int i = 0; i < nvalid; ++i) out[i] = v[i];
-          }
-        } else if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RES16) {
-          float *out = static_cast<float *>(g.out) + o;
-          for (int i = 0; i < nvalid; ++i) {
-            float x = v[i];
-            if constexpr (EPI == EPI_F32_RES16)
-              x = __fadd_rn(x, __half2float(static_cast<const __half *>(g.res)[o + i]));
-            out[i] = x;
-          }
-        } else if constexpr (EPI == EPI_F16_RES32) {
-          __half *out = static_cast<__half *>(g.out) + o;
-          const float *res = static_cast<const float *>(g.res) + o;
-          for (int i = 0; i < nvalid; ++i) out[i] = __float2half_rn(__fadd_rn(v[i], res[i]));
-        } else if constexpr (EPI == EPI_SWIGLU) {
-          // ldo counts output columns (inter); column pair (2i, 2i+1) -> output i.
-          __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
-          __align__(16) __half act[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            act[i] = __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(v[2 * i]))), v[2 * i + 1]));
-          if (nvalid == 16 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
-            *reinterpret_cast<uint4 *>(out) = *reinterpret_cast<const uint4 *>(act);
-          } else {
-            for (int i = 0; i + 1 < nvalid; i += 2) out[i / 2] = act[i / 2];
-          }
-        } else if constexpr (EPI == EPI_ARGMAX) {
-          for (int i = 0; i < nvalid; ++i)
-            if (v[i] > best) {
-              best = v[i];
-              best_i = col + i;
-            }
-        }
       }
-      if constexpr (EPI == EPI_ARGMAX) {
-        if (row < g.M) {
-          g.part_val[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best;
-          g.part_idx[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best_i;
-        }
+      if (row < g.M) {
+        g.part_val[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best;
+        g.part_idx[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best_i;
       }
+    } else if (ok) {
+      // The ring is idle (every copy landed, every MMA completed): each warp
+      // stages its 32 rows there, then stores them row-contiguously.
+      float *stg = reinterpret_cast<float *>(base) + q * (32 * EPI_PITCH);
+      if constexpr (EPI == EPI_SWIGLU2)
+        epilogue_swiglu2<BN>(g, tq, stg, m0 + 32 * q, n0, lane);
+      else
+        epilogue_staged<BN, EPI>(g, tq, stg, m0 + 32 * q, n0, lane);
     }
   }
+  // Lanes 1..31 of warps 0 and 1 skipped their roles' loops: they wait here
+  // for lane 0, so that each warp reaches the CTA barrier converged (a barrier
+  // counts whole warps, and tensor memory is freed only after it).
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (clustered) {
