@@ -53,7 +53,10 @@ int qwen_b200_swiglu_forward(const void *x, const void *w_gate, const void *w_up
 
 /* Bytes of device workspace qwen_b200_swiglu_forward_down(_ex) needs: the
  * SwiGLU activations, rows x inter fp16 (the fp16 chains) or their hi and lo
- * fp16 parts (the tensor-core path), so 4 bytes per element, rounded up to 256. */
+ * fp16 parts (the tensor-core path), so 4 bytes per element, rounded up to 256,
+ * then 12 bytes per element (rounded up to 256) for the tensor-core down
+ * projection's fp32 K slices (8 slices while hidden <= 3 inter / 8, fewer
+ * or a thread-block cluster reduction otherwise). */
 long long qwen_b200_swiglu_forward_down_workspace(long long rows, int inter);
 
 /* out[r, h] = b_down[h] + sum_i s[r,i] w_down[i,h] in fp16 steps, where s is
@@ -65,8 +68,9 @@ int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void 
                                   const void *b_down, void *out, void *workspace,
                                   long long rows, int hidden, int inter, void *stream);
 
-/* Bytes of device workspace qwen_b200_rmsnorm_swiglu_down(_ex) needs (the
- * normed rows when `normed` is NULL, then the activations as above). */
+/* Bytes of device workspace qwen_b200_rmsnorm_swiglu_down(_ex) needs: the
+ * normed rows (rows x hidden fp16, rounded up to 256; used when `normed` is
+ * NULL), then the activations and K slices as above. */
 long long qwen_b200_rmsnorm_swiglu_down_workspace(long long rows, int hidden, int inter);
 
 /* The config-3 chain in one call: normed = rmsnorm(x, norm_weight, eps,

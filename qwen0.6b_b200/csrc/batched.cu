@@ -89,12 +89,54 @@ __device__ __forceinline__ long long kv_row(const KvGeom &kg, int seq, int layer
   return ((static_cast<long long>(page) * kg.num_layers + layer) * NKV + g) * kg.page_tokens + off;
 }
 
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+// Lane `lane` of the warp that owns `row`: h = half(sum of the K slices of the
+// previous down projection (added in slice order) + res32) for the columns
+// 8 (lane + 32 j) .. +7, j < 4 -- the split-K reduction and residual of that
+// GEMM with the bits of splitk_reduce_kernel's EPI_F16_RES32.  The slices
+// are the outer loop so that each step issues all eight loads of the lane.
+__device__ __forceinline__ void reduce_down_row(const float *__restrict__ part, int splits,
+                                                const float *__restrict__ res32, int rows, int row, int lane,
+                                                uint4 (&v)[4]) {
+  const size_t slice4 = static_cast<size_t>(rows) * H / 4;
+  const float4 *p4 = reinterpret_cast<const float4 *>(part + static_cast<size_t>(row) * H);
+  const float4 *r4 = reinterpret_cast<const float4 *>(res32 + static_cast<size_t>(row) * H);
+  float4 a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = p4[2 * (lane + 32 * (i >> 1)) + (i & 1)];
+#pragma unroll 4
+  for (int z = 1; z < splits; ++z) {
+    float4 c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = p4[z * slice4 + 2 * (lane + 32 * (i >> 1)) + (i & 1)];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = add4(a[i], c[i]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 r0 = r4[2 * (lane + 32 * j)], r1 = r4[2 * (lane + 32 * j) + 1];
+    const float4 x = add4(a[2 * j], r0), y = add4(a[2 * j + 1], r1);
+    __half2 *h2 = reinterpret_cast<__half2 *>(&v[j]);
+    h2[0] = __floats2half2_rn(x.x, x.y);
+    h2[1] = __floats2half2_rn(x.z, x.w);
+    h2[2] = __floats2half2_rn(y.x, y.y);
+    h2[3] = __floats2half2_rn(y.z, y.w);
+  }
+}
+
 // ------------------------------------------------------------ input RMSNorm
 // xn = half(h * (inv * w)), inv = rsqrtf(sum(h^2) / 1024 + eps) (megakernel.cu:806-847).
-// Layer 0 gathers h = embed[token] and stores it as the row's hidden state.
+// Layer 0 gathers h = embed[token]; later layers, when the previous down
+// projection left K slices (`part`), first finish it: h = half(sum + res32).
+// h is stored as the row's hidden state.
 __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hidden,
                                                          const __half *__restrict__ embed,
                                                          const int *__restrict__ tokens,
+                                                         const float *__restrict__ part, int splits,
+                                                         const float *__restrict__ res32,
                                                          const __half *__restrict__ w,
                                                          __half *__restrict__ xn, int rows,
                                                          unsigned long long *err) {
@@ -116,6 +158,10 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
       v[j] = src[lane + 32 * j];
       reinterpret_cast<uint4 *>(hr)[lane + 32 * j] = v[j];
     }
+  } else if (part != nullptr) {
+    reduce_down_row(part, splits, res32, rows, row, lane, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) reinterpret_cast<uint4 *>(hr)[lane + 32 * j] = v[j];
   } else {
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] = reinterpret_cast<const uint4 *>(hr)[lane + 32 * j];
@@ -431,19 +477,48 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float *__restric
 
 // --------------------------------------------------- post-attention RMSNorm
 // sact = half(float(half(act)) * rstd * w), rstd from the fp32 act (megakernel.cu:614-638).
-__global__ void __launch_bounds__(256) post_norm_kernel(const float *__restrict__ act,
+// When the o_proj GEMM left K slices (`part`), this kernel finishes it first:
+// act = (sum of the slices in slice order) + float(res16), stored to `act`
+// (the bits of splitk_reduce_kernel's EPI_F32_RES16).
+__global__ void __launch_bounds__(256) post_norm_kernel(float *__restrict__ act,
+                                                        const float *__restrict__ part, int splits,
+                                                        const __half *__restrict__ res16,
                                                         const __half *__restrict__ w,
                                                         __half *__restrict__ sact, int rows) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const float4 *a4 = reinterpret_cast<const float4 *>(act + static_cast<size_t>(row) * H);
+  float4 *a4 = reinterpret_cast<float4 *>(act + static_cast<size_t>(row) * H);
   float4 v[8];
   float ss = 0.f;
+  if (part != nullptr) {
+    // Slices as the outer loop: each step issues all eight loads of the lane.
+    const size_t slice4 = static_cast<size_t>(rows) * H / 4;
+    const float4 *p4 = reinterpret_cast<const float4 *>(part + static_cast<size_t>(row) * H) + lane;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = p4[32 * j];
+#pragma unroll 4
+    for (int z = 1; z < splits; ++z) {
+      float4 c[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c[j] = p4[z * slice4 + 32 * j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = add4(v[j], c[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint2 ru = reinterpret_cast<const uint2 *>(res16 + static_cast<size_t>(row) * H)[lane + 32 * j];
+      const __half2 *r2 = reinterpret_cast<const __half2 *>(&ru);
+      v[j] = add4(v[j], make_float4(__low2float(r2[0]), __high2float(r2[0]), __low2float(r2[1]), __high2float(r2[1])));
+      a4[lane + 32 * j] = v[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = a4[lane + 32 * j];
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    v[j] = a4[lane + 32 * j];
     ss = fmaf(v[j].x, v[j].x, ss);
     ss = fmaf(v[j].y, v[j].y, ss);
     ss = fmaf(v[j].z, v[j].z, ss);
@@ -468,7 +543,9 @@ __global__ void __launch_bounds__(256) post_norm_kernel(const float *__restrict_
 // ------------------------------------------------------------ final RMSNorm
 // norm = (h * inv) * w in fp32 (megakernel.cu:890-919); norm16 = half(norm)
 // feeds the lm_head GEMM, norm32 (optional) is the caller's logits tap.
-__global__ void __launch_bounds__(256) final_norm_kernel(const __half *__restrict__ hidden,
+__global__ void __launch_bounds__(256) final_norm_kernel(__half *__restrict__ hidden,
+                                                         const float *__restrict__ part, int splits,
+                                                         const float *__restrict__ res32,
                                                          const __half *__restrict__ w,
                                                          __half *__restrict__ norm16,
                                                          float *__restrict__ norm32, int rows) {
@@ -476,12 +553,19 @@ __global__ void __launch_bounds__(256) final_norm_kernel(const __half *__restric
   qb200::griddep_launch_dependents();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const __half *hr = hidden + static_cast<size_t>(row) * H;
+  __half *hr = hidden + static_cast<size_t>(row) * H;
   uint4 v[4];
   float ss = 0.f;
+  if (part != nullptr) {  // the last down projection's K slices (as input_norm_kernel)
+    reduce_down_row(part, splits, res32, rows, row, lane, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) reinterpret_cast<uint4 *>(hr)[lane + 32 * j] = v[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = reinterpret_cast<const uint4 *>(hr)[lane + 32 * j];
+  }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    v[j] = reinterpret_cast<const uint4 *>(hr)[lane + 32 * j];
     const __half2 *h2 = reinterpret_cast<const __half2 *>(&v[j]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -759,6 +843,23 @@ int run_proj(Plan *p, int i, const GemmPlan &gp, int epi, const GemmArgs &g, flo
   return qb200_gemm_run(gp, epi, g, st);
 }
 
+// Projection i split over K into fp32 slices [ksplit][rows][N] at `partial`
+// and left unreduced: the next kernel adds the slices (in slice order) and
+// the residual, as splitk_reduce_kernel would have.  True when it did so;
+// false (nothing launched) when projection i is not split that way.
+bool run_proj_slices(Plan *p, int i, const GemmPlan &gp, const GemmArgs &g, float *partial, cudaStream_t st,
+                     int *rc) {
+  *rc = 0;
+  if (p->ksplit[i] < 2 || p->kcluster[i]) return false;
+  GemmArgs gs = g;
+  gs.out = partial;
+  gs.ldo = gp.N;
+  gs.res = nullptr;
+  gs.k_splits = p->ksplit[i];
+  *rc = qb200_gemm_run(gp, qb200tc::EPI_PARTIAL, gs, st);
+  return true;
+}
+
 // Every layer of a step plus the final RMSNorm (w.norm16 feeds the lm_head).
 int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, const int *tokens_in,
                 float *norm_out, int max_position, float attn_scale, cudaStream_t st) {
@@ -775,10 +876,15 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     const cudaError_t le = qb200_launch(kernel, grid, block, smem_bytes, st, true, __VA_ARGS__); \
     if (le != cudaSuccess) return fail(20, "%s launch: %s", #kernel, cudaGetErrorString(le));   \
   } while (0)
+  // The o_proj and down projections split over K leave their slices to the
+  // following norm kernel (post-attention norm, next layer's input norm or
+  // the final norm), which finishes the reduction and the residual.
+  const float *down_part = nullptr;  // slices of the previous layer's down projection
   for (int l = 0; l < p->num_layers; ++l) {
     const QwenBatchedLayer &L = p->layers[l];
     LAUNCH(input_norm_kernel, dim3(nb8), dim3(256), 0, w.hidden, l == 0 ? p->embed : nullptr,
-           tokens_in, static_cast<const __half *>(L.input_norm), w.xn, rows, w.err);
+           tokens_in, down_part, p->ksplit[3], static_cast<const float *>(w.act),
+           static_cast<const __half *>(L.input_norm), w.xn, rows, w.err);
     GemmArgs g{};
     g.M = rows;
     g.err = w.err;
@@ -799,9 +905,13 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     g.out = w.act;
     g.ldo = H;
     g.res = w.hidden;
-    if (int rc = run_proj(p, 1, p->g_o[l], qb200tc::EPI_F32_RES16, g, w.splitk, st)) return rc;
-    LAUNCH(post_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const float *>(w.act),
-           static_cast<const __half *>(L.post_norm), w.sact, rows);
+    int rc = 0;
+    const bool o_sliced = run_proj_slices(p, 1, p->g_o[l], g, w.splitk, st, &rc);
+    if (rc) return rc;
+    if (!o_sliced && (rc = run_proj(p, 1, p->g_o[l], qb200tc::EPI_F32_RES16, g, w.splitk, st))) return rc;
+    LAUNCH(post_norm_kernel, dim3(nb8), dim3(256), 0, w.act,
+           o_sliced ? static_cast<const float *>(w.splitk) : nullptr, p->ksplit[1],
+           static_cast<const __half *>(w.hidden), static_cast<const __half *>(L.post_norm), w.sact, rows);
     g.out = w.inter;
     g.ldo = IM;
     g.res = nullptr;
@@ -809,10 +919,13 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     g.out = w.hidden;
     g.ldo = H;
     g.res = w.act;
-    if (int rc = run_proj(p, 3, p->g_down[l], qb200tc::EPI_F16_RES32, g, w.splitk, st)) return rc;
+    const bool down_sliced = run_proj_slices(p, 3, p->g_down[l], g, w.splitk, st, &rc);
+    if (rc) return rc;
+    if (!down_sliced && (rc = run_proj(p, 3, p->g_down[l], qb200tc::EPI_F16_RES32, g, w.splitk, st))) return rc;
+    down_part = down_sliced ? w.splitk : nullptr;
   }
-  LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, static_cast<const __half *>(w.hidden),
-         p->final_norm, w.norm16, norm_out, rows);
+  LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, w.hidden, down_part, p->ksplit[3],
+         static_cast<const float *>(w.act), p->final_norm, w.norm16, norm_out, rows);
 #undef LAUNCH
   return 0;
 }

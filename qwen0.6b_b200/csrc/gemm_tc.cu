@@ -49,10 +49,12 @@ __global__ void argmax_reduce_kernel(const float *__restrict__ part_val,
 }
 
 // Split-K reduction: sum the k_splits fp32 partial slices in slice order and
-// apply the final epilogue.  Thread = 4 consecutive columns of one row.
+// apply the final epilogue (EPI_F16: + bias in fp32 when given, as the GEMM
+// epilogue).  Thread = 4 consecutive columns of one row.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restrict__ part,
                                                             int splits, int M, int N, int epi,
                                                             const void *__restrict__ res,
+                                                            const __half *__restrict__ bias,
                                                             void *__restrict__ out, int ldo) {
   qb200::griddep_wait();
   qb200::griddep_launch_dependents();
@@ -92,7 +94,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float *__restr
   } else if (epi == EPI_F32) {
     *reinterpret_cast<float4 *>(static_cast<float *>(out) + o) = acc;
   } else {  // EPI_F16
-    __half2 h[2] = {__floats2half2_rn(a[0], a[1]), __floats2half2_rn(a[2], a[3])};
+    float b[4] = {a[0], a[1], a[2], a[3]};
+    if (bias != nullptr)
+      for (int i = 0; i < 4; ++i) b[i] = __fadd_rn(b[i], __half2float(bias[col + i]));
+    __half2 h[2] = {__floats2half2_rn(b[0], b[1]), __floats2half2_rn(b[2], b[3])};
     *reinterpret_cast<uint2 *>(static_cast<__half *>(out) + o) = *reinterpret_cast<const uint2 *>(h);
   }
 }
@@ -226,6 +231,7 @@ int launch_bn_mn(int epi, const GemmPlan &p, const GemmArgs &g, cudaStream_t st)
   switch (epi) {
     case EPI_F16: return launch_t<BN, EPI_F16, BL_MN>(p.ma, p.mb, p.mb, g, st);
     case EPI_F32: return launch_t<BN, EPI_F32, BL_MN>(p.ma, p.mb, p.mb, g, st);
+    case EPI_PARTIAL: return launch_t<BN, EPI_PARTIAL, BL_MN>(p.ma, p.mb, p.mb, g, st);
     default: return fail(10, "epilogue %d is not built for an MN-major B", epi);
   }
 }
@@ -325,7 +331,8 @@ int qb200_gemm_run_splitk(const GemmPlan &p, int epi, GemmArgs g, int splits, fl
   const long long threads = static_cast<long long>(M) * (p.N / 4);
   const cudaError_t e = qb200_launch(splitk_reduce_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)),
                                      dim3(256), 0, st, g.pdl != 0, static_cast<const float *>(partial),
-                                     splits, M, p.N, epi, g.res, g.out, g.ldo);
+                                     splits, M, p.N, epi, g.res, static_cast<const __half *>(g.bias), g.out,
+                                     g.ldo);
   if (e != cudaSuccess) return fail(20, "split-K reduce launch: %s", cudaGetErrorString(e));
   return 0;
 }

@@ -294,10 +294,9 @@ template <int EPI>
 constexpr bool kEpiF16Out = EPI == EPI_F16 || EPI == EPI_F16_RES32 || EPI == EPI_SWIGLU;
 
 // Eight consecutive outputs x[0..7] of one row at element offset o: the
-// epilogue's last step (residual, rounding) and the store, as two or one
-// 16-byte accesses when `vec`, else element by element.
+// residual of the epilogue added in fp32 (16-byte loads when `vec`).
 template <int EPI>
-__device__ __forceinline__ void store_unit8(const GemmArgs &g, size_t o, float (&x)[8], bool vec) {
+__device__ __forceinline__ void add_residual8(const GemmArgs &g, size_t o, float (&x)[8], bool vec) {
   if constexpr (EPI == EPI_F32_RES16) {
     const __half *r = static_cast<const __half *>(g.res) + o;
     if (vec) {
@@ -324,6 +323,12 @@ __device__ __forceinline__ void store_unit8(const GemmArgs &g, size_t o, float (
       for (int i = 0; i < 8; ++i) x[i] = __fadd_rn(x[i], r[i]);
     }
   }
+}
+
+// The same eight outputs rounded to the output type and stored: one or two
+// 16-byte stores when `vec`, else element by element.
+template <int EPI>
+__device__ __forceinline__ void store_unit8(const GemmArgs &g, size_t o, const float (&x)[8], bool vec) {
   if constexpr (kEpiF16Out<EPI>) {
     __half *out = static_cast<__half *>(g.out) + o;
     if (vec) {
@@ -392,18 +397,40 @@ __device__ __forceinline__ void epilogue_staged(const GemmArgs &g, uint32_t tq, 
     for (int i = 0; i < OUTS / 4; ++i)
       reinterpret_cast<float4 *>(srow)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     __syncwarp();
-#pragma unroll 1
-    for (int u = lane; u < 32 * UPR; u += 32) {
-      const int r = u / UPR, j = u % UPR;
+    // Lane l takes the units l, l + 32, ... (unit u = row u / UPR, outputs
+    // 8 (u % UPR) ..): every staged value and residual is loaded before the
+    // first store, so the loads are not serialised behind the stores.
+    float x[UPR][8];
+    bool ok[UPR];
+#pragma unroll
+    for (int t = 0; t < UPR; ++t) {
+      const int u = lane + 32 * t, r = u / UPR, j = u % UPR;
       const int row = rbase + r, oc = oc0 + 8 * j;
-      if (row >= g.M || oc >= nout) continue;
+      ok[t] = row < g.M && oc < nout;
       const float4 *s4 = reinterpret_cast<const float4 *>(stg + r * EPI_PITCH) + 2 * j;
       const float4 a = s4[0], b = s4[1];
-      float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-      store_unit8<EPI>(g, static_cast<size_t>(row) * g.ldo + oc, x, vec);
+      x[t][0] = a.x; x[t][1] = a.y; x[t][2] = a.z; x[t][3] = a.w;
+      x[t][4] = b.x; x[t][5] = b.y; x[t][6] = b.z; x[t][7] = b.w;
+      if (ok[t]) add_residual8<EPI>(g, static_cast<size_t>(row) * g.ldo + oc, x[t], vec);
     }
     __syncwarp();  // the staging rows are rewritten by the next chunk
+#pragma unroll
+    for (int t = 0; t < UPR; ++t) {
+      const int u = lane + 32 * t, r = u / UPR, j = u % UPR;
+      if (ok[t]) store_unit8<EPI>(g, static_cast<size_t>(rbase + r) * g.ldo + oc0 + 8 * j, x[t], vec);
+    }
   }
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Eight halves into dst: one 16-byte store when `vec`, else element by element.
@@ -445,52 +472,73 @@ __device__ __forceinline__ void epilogue_swiglu2(const GemmArgs &g, uint32_t tq,
     float v[64];
     tmem_ld64(tq + c0, tq + BN / 2 + c0, v);
     const int nv = min(32, nout - oc0);
+    if (bias != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) v[i] = __fadd_rn(v[i], __half2float(bias[oc0 + i]));
+    }
+    if (bias2 != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < nv) v[32 + i] = __fadd_rn(v[32 + i], __half2float(bias2[oc0 + i]));
+    }
+    if (out2 != nullptr || out3 != nullptr) {  // the gate / up caches are staged only when asked for
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        reinterpret_cast<float4 *>(srow + 32)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        reinterpret_cast<float4 *>(srow + 64)[i] =
+            make_float4(v[32 + 4 * i], v[33 + 4 * i], v[34 + 4 * i], v[35 + 4 * i]);
+      }
+    }
+    // s = g * u * 1 / (1 + 2^(-g log2 e)) with one ex2.approx and one
+    // rcp.approx per output (relative errors ~2^-22 and 1 ulp, plus |g| 2^-24
+    // from the scaled argument): branch-free, so the 32 outputs overlap.  The
+    // library exp and IEEE division each carry special-case branches that
+    // serialised them (2.4 - 12 us per tile).  g -> -inf gives 2^+inf = inf
+    // and a reciprocal of 0, so s = 0.  Far inside the fp16 ulp (2^-11) of
+    // the stored hi part; the lo part carries the rest to ~2^-21.
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float gg = (bias != nullptr && i < nv) ? __fadd_rn(v[i], __half2float(bias[oc0 + i])) : v[i];
-      const float uu = (bias2 != nullptr && i < nv) ? __fadd_rn(v[32 + i], __half2float(bias2[oc0 + i])) : v[32 + i];
-      v[i] = gg;
-      v[32 + i] = uu;
+      const float e = ex2_approx(__fmul_rn(v[i], -1.4426950408889634f));
+      v[i] = __fmul_rn(__fmul_rn(v[i], v[32 + i]), rcp_approx(__fadd_rn(1.0f, e)));
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      reinterpret_cast<float4 *>(srow + 32)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      reinterpret_cast<float4 *>(srow + 64)[i] =
-          make_float4(v[32 + 4 * i], v[33 + 4 * i], v[34 + 4 * i], v[35 + 4 * i]);
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), v[32 + i]);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       reinterpret_cast<float4 *>(srow)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     __syncwarp();
-#pragma unroll 1
-    for (int u = lane; u < 32 * 4; u += 32) {
-      const int r = u >> 2, j = u & 3;
-      const int row = rbase + r, oc = oc0 + 8 * j;
-      if (row >= g.M || oc >= nout) continue;
-      const float *sr = stg + r * EPI_PITCH + 8 * j;
-      float s[8], lo[8];
+    // Lane l takes the units l, l + 32, l + 64, l + 96 (row u / 4, outputs
+    // 8 (u % 4) ..), all staged values loaded before the first store.
+    const bool caches = out2 != nullptr || out3 != nullptr;
+    float sv[4][8], gv[4][8], uv[4][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        s[i] = sr[i];
-        lo[i] = __fsub_rn(s[i], __half2float(__float2half_rn(s[i])));
-      }
-      const size_t o = static_cast<size_t>(row) * g.ldo + oc;
-      put_half8(out + o, s, vec);
-      if (g.lo_col > 0) put_half8(out + o + g.lo_col, lo, vec);
-      if (out2 != nullptr || out3 != nullptr) {
-        float gg[8], uu[8];
+    for (int t = 0; t < 4; ++t) {
+      const int u = lane + 32 * t, r = u >> 2, j = u & 3;
+      const float *sr = stg + r * EPI_PITCH + 8 * j;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sv[t][i] = sr[i];
+      if (caches) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          gg[i] = sr[32 + i];
-          uu[i] = sr[64 + i];
+          gv[t][i] = sr[32 + i];
+          uv[t][i] = sr[64 + i];
         }
-        if (out2 != nullptr) put_half8(out2 + o, gg, vec);
-        if (out3 != nullptr) put_half8(out3 + o, uu, vec);
       }
     }
     __syncwarp();  // the staging rows are rewritten by the next chunk
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int u = lane + 32 * t, r = u >> 2, j = u & 3;
+      const int row = rbase + r, oc = oc0 + 8 * j;
+      if (row >= g.M || oc >= nout) continue;
+      float lo[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lo[i] = __fsub_rn(sv[t][i], __half2float(__float2half_rn(sv[t][i])));
+      const size_t o = static_cast<size_t>(row) * g.ldo + oc;
+      put_half8(out + o, sv[t], vec);
+      if (g.lo_col > 0) put_half8(out + o + g.lo_col, lo, vec);
+      if (out2 != nullptr) put_half8(out2 + o, gv[t], vec);
+      if (out3 != nullptr) put_half8(out3 + o, uv[t], vec);
+    }
   }
 }
 
@@ -661,7 +709,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         g.part_val[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best;
         g.part_idx[static_cast<size_t>(row) * g.n_tiles + blockIdx.x] = best_i;
       }
-    } else if (ok) {
+    } else if (ok && m0 + 32 * q < g.M) {  // (a warp whose 32 rows are all past M has nothing to do)
       // The ring is idle (every copy landed, every MMA completed): each warp
       // stages its 32 rows there, then stores them row-contiguously.
       float *stg = reinterpret_cast<float *>(base) + q * (32 * EPI_PITCH);
@@ -691,55 +739,69 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp >= 2 && !*abort) {
       constexpr int C4 = BN / 4;
       const int t = threadIdx.x - 64;  // 0..127
-      for (int idx = t; idx < (r1 - r0) * C4; idx += 128) {
-        const int lrow = r0 + idx / C4, c = 4 * (idx % C4);
-        const int row = m0 + lrow, col = n0 + c;
-        if (row >= g.M || col >= g.N) continue;
-        const uint32_t trow = smem_u32(base) + static_cast<uint32_t>(lrow * TPITCH) * 4u;
-        float4 pz[8];
+      // Two entries per thread and step, every distributed-shared-memory load
+      // of both issued before the first add (one round trip per step).
+      const int count = (r1 - r0) * C4;
+      for (int i0 = t; i0 < count; i0 += 256) {
+        float4 pz[2][8];
 #pragma unroll
-        for (int z = 0; z < 8; ++z)
-          if (z < Z) pz[z] = ld_dsmem_f4(map_rank(trow + c * 4, z));
-        float4 acc = pz[0];
+        for (int u = 0; u < 2; ++u) {
+          const int idx = i0 + 128 * u;
+          if (idx >= count) continue;
+          const int lrow = r0 + idx / C4, c = 4 * (idx % C4);
+          const uint32_t trow = smem_u32(base) + static_cast<uint32_t>(lrow * TPITCH) * 4u;
 #pragma unroll
-        for (int z = 1; z < 8; ++z) {
-          if (z < Z) {
-            acc.x = __fadd_rn(acc.x, pz[z].x);
-            acc.y = __fadd_rn(acc.y, pz[z].y);
-            acc.z = __fadd_rn(acc.z, pz[z].z);
-            acc.w = __fadd_rn(acc.w, pz[z].w);
-          }
+          for (int z = 0; z < 8; ++z)
+            if (z < Z) pz[u][z] = ld_dsmem_f4(map_rank(trow + c * 4, z));
         }
-        const size_t o = static_cast<size_t>(row) * g.ldo + col;
-        if constexpr (EPI == EPI_F32_RES16) {
-          const __half *r = static_cast<const __half *>(g.res) + o;
-          *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) =
-              make_float4(__fadd_rn(acc.x, __half2float(r[0])), __fadd_rn(acc.y, __half2float(r[1])),
-                          __fadd_rn(acc.z, __half2float(r[2])), __fadd_rn(acc.w, __half2float(r[3])));
-        } else if constexpr (EPI == EPI_F16_RES32) {
-          const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(g.res) + o);
-          __half2 h[2] = {__floats2half2_rn(__fadd_rn(acc.x, r.x), __fadd_rn(acc.y, r.y)),
-                          __floats2half2_rn(__fadd_rn(acc.z, r.z), __fadd_rn(acc.w, r.w))};
-          *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
-        } else if constexpr (EPI == EPI_F32) {
-          *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) = acc;
-        } else if constexpr (EPI == EPI_SWIGLU) {
-          // Column pairs (gate, up) -> output column col / 2 (ldo counts outputs).
-          __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
-          __half2 h = __halves2half2(
-              __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.x))), acc.y)),
-              __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.z))), acc.w)));
-          *reinterpret_cast<__half2 *>(out) = h;
-        } else if constexpr (EPI == EPI_F16) {
-          if (g.bias != nullptr) {
-            const __half *b = static_cast<const __half *>(g.bias) + col;
-            acc.x = __fadd_rn(acc.x, __half2float(b[0]));
-            acc.y = __fadd_rn(acc.y, __half2float(b[1]));
-            acc.z = __fadd_rn(acc.z, __half2float(b[2]));
-            acc.w = __fadd_rn(acc.w, __half2float(b[3]));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int idx = i0 + 128 * u;
+          if (idx >= count) continue;
+          const int lrow = r0 + idx / C4, c = 4 * (idx % C4);
+          const int row = m0 + lrow, col = n0 + c;
+          if (row >= g.M || col >= g.N) continue;
+          float4 acc = pz[u][0];
+#pragma unroll
+          for (int z = 1; z < 8; ++z) {
+            if (z < Z) {
+              acc.x = __fadd_rn(acc.x, pz[u][z].x);
+              acc.y = __fadd_rn(acc.y, pz[u][z].y);
+              acc.z = __fadd_rn(acc.z, pz[u][z].z);
+              acc.w = __fadd_rn(acc.w, pz[u][z].w);
+            }
           }
-          __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
-          *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+          const size_t o = static_cast<size_t>(row) * g.ldo + col;
+          if constexpr (EPI == EPI_F32_RES16) {
+            const __half *r = static_cast<const __half *>(g.res) + o;
+            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) =
+                make_float4(__fadd_rn(acc.x, __half2float(r[0])), __fadd_rn(acc.y, __half2float(r[1])),
+                            __fadd_rn(acc.z, __half2float(r[2])), __fadd_rn(acc.w, __half2float(r[3])));
+          } else if constexpr (EPI == EPI_F16_RES32) {
+            const float4 r = *reinterpret_cast<const float4 *>(static_cast<const float *>(g.res) + o);
+            __half2 h[2] = {__floats2half2_rn(__fadd_rn(acc.x, r.x), __fadd_rn(acc.y, r.y)),
+                            __floats2half2_rn(__fadd_rn(acc.z, r.z), __fadd_rn(acc.w, r.w))};
+            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+          } else if constexpr (EPI == EPI_F32) {
+            *reinterpret_cast<float4 *>(static_cast<float *>(g.out) + o) = acc;
+          } else if constexpr (EPI == EPI_SWIGLU) {
+            // Column pairs (gate, up) -> output column col / 2 (ldo counts outputs).
+            __half *out = static_cast<__half *>(g.out) + static_cast<size_t>(row) * g.ldo + col / 2;
+            __half2 h = __halves2half2(
+                __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.x))), acc.y)),
+                __float2half_rn(__fmul_rn(__half2float(silu_half(__float2half_rn(acc.z))), acc.w)));
+            *reinterpret_cast<__half2 *>(out) = h;
+          } else if constexpr (EPI == EPI_F16) {
+            if (g.bias != nullptr) {
+              const __half *b = static_cast<const __half *>(g.bias) + col;
+              acc.x = __fadd_rn(acc.x, __half2float(b[0]));
+              acc.y = __fadd_rn(acc.y, __half2float(b[1]));
+              acc.z = __fadd_rn(acc.z, __half2float(b[2]));
+              acc.w = __fadd_rn(acc.w, __half2float(b[3]));
+            }
+            __half2 h[2] = {__floats2half2_rn(acc.x, acc.y), __floats2half2_rn(acc.z, acc.w)};
+            *reinterpret_cast<uint2 *>(static_cast<__half *>(g.out) + o) = *reinterpret_cast<const uint2 *>(h);
+          }
         }
       }
     }

@@ -480,6 +480,13 @@ int check_swiglu(const void *x, const void *wg, const void *wu, const void *wd, 
 
 long long round256(long long b) { return (b + 255) & ~255ll; }
 
+// SwiGLU + down workspace: the activations (fp16 s for the chains, its hi |
+// lo parts for the tensor cores), then room for the down projection's fp32 K
+// slices: 12 bytes per activation, i.e. 8 slices whenever hidden <= 3 inter / 8
+// (Qwen3-0.6B: hidden = inter / 3).
+long long swiglu_ws_act(long long rows, int inter) { return round256(rows * inter * 4); }
+long long swiglu_ws_part(long long rows, int inter) { return round256(rows * inter * 12); }
+
 int rmsnorm_launch(void *out, float *rms, const void *input, const void *weight, void *residual,
                    long long rows, int cols, float eps, cudaStream_t st) {
   if (rows < 0 || cols <= 0) return fail(10, "rows=%lld cols=%d out of range", rows, cols);
@@ -540,11 +547,13 @@ bool tc_shape_ok(int hidden, int inter) { return hidden % 64 == 0 && inter % 64 
 // The gate|up GEMM holds 64 gate and 64 up columns per 128-column tile and
 // stores s as fp16 hi = half(s) and lo = half(s - hi) ([rows, 2 inter] in
 // sbuf); the down GEMM runs over K = 2 inter ([hi | lo] against w_down read
-// twice), so s enters it with ~22 significant bits, and splits K over a
-// thread-block cluster (no workspace).
+// twice), so s enters it with ~22 significant bits, and splits K into fp32
+// slices in `part` (part_bytes) added by a reduction kernel -- or, when they
+// do not fit there, over a thread-block cluster, which measured slower (18 us
+// against 10 us at 64 rows, 14 against 12.5 at 256).
 int swiglu_down_tc(const void *x, const void *wg, const void *wu, const void *wd, const void *bg,
-                   const void *bu, const void *bd, void *sbuf, void *out, long long rows, int hidden,
-                   int inter, cudaStream_t st) {
+                   const void *bu, const void *bd, void *sbuf, float *part, long long part_bytes, void *out,
+                   long long rows, int hidden, int inter, cudaStream_t st) {
   const int M = static_cast<int>(rows);
   GemmPlan p1{};
   if (int rc = qb200_gemm_make_maps_mn(&p1, x, wg, wu, M, inter, hidden, hidden, inter, 128)) return rc;
@@ -568,9 +577,13 @@ int swiglu_down_tc(const void *x, const void *wg, const void *wu, const void *wd
   g2.ldo = hidden;
   g2.bias = bd;
   g2.b_kwrap = inter / qb200tc::BK;
+  // 64-column tiles (128-column ones with 8 slices measured slower).
+  const int nk = 2 * inter / qb200tc::BK;
+  for (int splits : {8, 4, 2})
+    if (splits <= nk && static_cast<long long>(splits) * M * hidden * 4 <= part_bytes)
+      return qb200_gemm_run_splitk(p2, qb200tc::EPI_F16, g2, splits, part, st);
   const int tiles = (hidden / 64) * ((M + qb200tc::BM - 1) / qb200tc::BM);
-  const int splits = tiles >= 32 ? 4 : 8;
-  return qb200_gemm_run_splitk(p2, qb200tc::EPI_F16, g2, splits, nullptr, st);
+  return qb200_gemm_run_splitk(p2, qb200tc::EPI_F16, g2, min(nk, tiles >= 32 ? 4 : 8), nullptr, st);
 }
 
 }  // namespace
@@ -653,7 +666,7 @@ int qwen_b200_swiglu_forward(const void *x, const void *w_gate, const void *w_up
 
 long long qwen_b200_swiglu_forward_down_workspace(long long rows, int inter) {
   if (rows < 0 || inter < 0) return 0;
-  return round256(rows * inter * 4);  // fp16 s (chains) or its hi | lo parts (tensor cores)
+  return swiglu_ws_act(rows, inter) + swiglu_ws_part(rows, inter);
 }
 
 int qwen_b200_swiglu_forward_down(const void *x, const void *w_gate, const void *w_up,
@@ -692,8 +705,9 @@ int qwen_b200_swiglu_forward_down_ex(const void *x, const void *w_gate, const vo
   if (w_down == nullptr || out == nullptr || workspace == nullptr)
     return fail(13, "null pointer argument");
   if (!al16(out) || !al16(workspace)) return fail(14, "SwiGLU operands must be 16-byte aligned");
-  return swiglu_down_tc(x, w_gate, w_up, w_down, b_gate, b_up, b_down, workspace, out, rows, hidden,
-                        inter, static_cast<cudaStream_t>(stream));
+  float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + swiglu_ws_act(rows, inter));
+  return swiglu_down_tc(x, w_gate, w_up, w_down, b_gate, b_up, b_down, workspace, part,
+                        swiglu_ws_part(rows, inter), out, rows, hidden, inter, static_cast<cudaStream_t>(stream));
 }
 
 int qwen_b200_rmsnorm_swiglu_down_ex(const void *x, const void *norm_weight, void *residual,
@@ -726,13 +740,14 @@ int qwen_b200_rmsnorm_swiglu_down_ex(const void *x, const void *norm_weight, voi
   void *nbuf = normed != nullptr ? normed : ws;
   void *sbuf = ws + round256(rows * hidden * 2);
   if (int rc = rmsnorm_launch(nbuf, rms, x, norm_weight, residual, rows, hidden, eps, st)) return rc;
-  return swiglu_down_tc(nbuf, w_gate, w_up, w_down, b_gate, b_up, b_down, sbuf, out, rows, hidden,
-                        inter, st);
+  float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(sbuf) + swiglu_ws_act(rows, inter));
+  return swiglu_down_tc(nbuf, w_gate, w_up, w_down, b_gate, b_up, b_down, sbuf, part, swiglu_ws_part(rows, inter),
+                        out, rows, hidden, inter, st);
 }
 
 long long qwen_b200_rmsnorm_swiglu_down_workspace(long long rows, int hidden, int inter) {
   if (rows < 0 || hidden < 0 || inter < 0) return 0;
-  return round256(rows * hidden * 2) + round256(rows * inter * 4);
+  return round256(rows * hidden * 2) + swiglu_ws_act(rows, inter) + swiglu_ws_part(rows, inter);
 }
 
 int qwen_b200_rmsnorm_swiglu_down(const void *x, const void *norm_weight, void *residual,

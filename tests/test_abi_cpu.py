@@ -109,8 +109,10 @@ def test_swiglu_rejects_bad_arguments(rows, hidden, inter, misalign, pattern):
 
 def test_ops_workspace_and_empty_calls():
     lib = _ops_lib()
-    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 3072) == 3 * 3072 * 4
-    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 40) == 512
+    # activations (4 bytes per element) + the down projection's K slices
+    # (12 bytes per element), each rounded up to 256 bytes
+    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 3072) == 3 * 3072 * 4 + 3 * 3072 * 12
+    assert lib.qwen_b200_swiglu_forward_down_workspace(3, 40) == 512 + 1536
     # Empty inputs are a no-op (no CUDA call), even with null pointers.
     assert lib.qwen_b200_swiglu_forward(*([None] * 8), 0, 1024, 3072, None) == 0
     assert lib.qwen_b200_rmsnorm_forward(*([None] * 5), 0, 1024, 1e-6, None) == 0
