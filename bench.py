@@ -655,6 +655,8 @@ def lmhead_line(args, world: int, rank: int, local: int, dev, dist, B: int, with
     g = torch.Generator(device=dev).manual_seed(SEED)
     emb = (0.02 * torch.randn(VOCAB, HIDDEN, generator=g, device=dev)).half()
     x = torch.randn(B, HIDDEN, generator=g, device=dev).half()
+    # The unsharded argmax on this GPU: the sharded tokens must equal it bit for bit.
+    unsharded = ShardedLMHead(emb, 1, 0, device=dev, max_rows=B).argmax(x).clone() if world > 1 else None
     head = ShardedLMHead(emb, world, rank, device=dev, max_rows=B, exchange=args.exchange)
     del emb
     torch.cuda.empty_cache()
@@ -682,6 +684,8 @@ def lmhead_line(args, world: int, rank: int, local: int, dev, dist, B: int, with
         torch.cuda.cudart().cudaProfilerStop()
     clk = clocks.stop()
     assert torch.equal(tok, ref), "non-deterministic sharded argmax"
+    if unsharded is not None:
+        assert torch.equal(tok, unsharded), "sharded argmax differs from the unsharded one"
     total_ms = t_start.elapsed_time(t_end)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     # End to end: hidden rows from pinned host memory, tokens back to the host.
@@ -719,7 +723,8 @@ def lmhead_line(args, world: int, rank: int, local: int, dev, dist, B: int, with
                                   if head.exchange == "peer" else "all-gathered over NCCL"),
                    "batch": B, "parallelism": f"vocab shards x{world}" if world > 1 else "single GPU",
                    "l2": f"weights of a shard ({(head.hi - head.lo) * HIDDEN * 2 / 1e6:.1f} MB) are re-read "
-                         "each step; no flush" + (" (a shard fits in L2 at 8 GPUs)" if world >= 4 else "")},
+                         "each step; no flush" + (" (a shard fits in L2 at 8 GPUs)" if world >= 4 else ""),
+                   "tokens": "equal to the unsharded argmax on every rank" if world > 1 else "single shard"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_src": peaks["src"], "traffic": None,
                      "algorithmic_bytes_per_step": shard_bytes, "avg_step_ms": avg_step_s * 1000.0},
