@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
                                                          unsigned long long *err) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   __half *hr = hidden + static_cast<size_t>(row) * H;
   uint4 v[4];
@@ -198,11 +198,11 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
 }
 
 // ------------------------------------------------ q/k RMSNorm, RoPE, KV append
-// Per row (one CTA of 256 threads): 16 q heads and 8 k heads normalised over
+// Per row (one CTA, one warp per head): 16 q heads and 8 k heads normalised over
 // 128 dims (eps 1e-6, (x * inv) * w) and rotated (rotate-half, fp16 cos/sin
 // tables), rounded to fp16 (megakernel.cu:339-434); rotated K and raw V go to
 // the caches at the row's position.
-__global__ void __launch_bounds__(256) qk_rope_kv_kernel(
+__global__ void __launch_bounds__(32 * (NQ + NKV)) qk_rope_kv_kernel(
     const __half *__restrict__ qkv, const __half *__restrict__ q_norm,
     const __half *__restrict__ k_norm, const __half *__restrict__ cos_t,
     const __half *__restrict__ sin_t, const int *__restrict__ seq_ids,
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
   const __half *src_row = qkv + static_cast<size_t>(row) * QKV;
   const __half *cosp = cos_t + static_cast<size_t>(pos) * HD;
   const __half *sinp = sin_t + static_cast<size_t>(pos) * HD;
-  for (int hh = warp; hh < NQ + NKV; hh += 8) {
+  for (int hh = warp; hh < NQ + NKV; hh += blockDim.x >> 5) {  // one warp per head at launch size
     const bool is_q = hh < NQ;
     const __half *src = src_row + (is_q ? hh * HD : QS + (hh - NQ) * HD);
     const __half *nw = is_q ? q_norm : k_norm;
@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(256) qk_rope_kv_kernel(
       dst[i] = __float2half_rn(r);
     }
   }
-  // V (raw) into the cache: thread t copies elements 4t .. 4t+3.
+  // V (raw) into the cache: thread t < 256 copies elements 4t .. 4t+3.
+  if (threadIdx.x >= KVS / 4) return;
   const int e = 4 * threadIdx.x, g = e / HD, d = e % HD;
   const uint2 val = *reinterpret_cast<const uint2 *>(src_row + QS + KVS + e);
   *reinterpret_cast<uint2 *>(v_pool + static_cast<size_t>(row0) * HD + g * head_stride + d) = val;
@@ -487,7 +488,7 @@ __global__ void __launch_bounds__(256) post_norm_kernel(float *__restrict__ act,
                                                         __half *__restrict__ sact, int rows) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   float4 *a4 = reinterpret_cast<float4 *>(act + static_cast<size_t>(row) * H);
   float4 v[8];
@@ -551,7 +552,7 @@ __global__ void __launch_bounds__(256) final_norm_kernel(__half *__restrict__ hi
                                                          float *__restrict__ norm32, int rows) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   __half *hr = hidden + static_cast<size_t>(row) * H;
   uint4 v[4];
@@ -673,10 +674,11 @@ struct Plan {
   CUtensorMap tm_k;   // K pool as [pages * layers * 8 * page_tokens rows, 128], 64 x CH boxes, 128B swizzle
 };
 
-int lm_tiles_for(int max_rows) {
-  const int bn = qb200_gemm_bn(max_rows, VOCAB);
-  return (VOCAB + bn - 1) / bn;
-}
+// The lm_head GEMM takes 256-column tiles: the 151,936-row embedding is
+// the one operand that matters, and wider tiles re-read the activation rows
+// half as often.
+constexpr int LM_BN = 256;
+int lm_tiles_for(int) { return (VOCAB + LM_BN - 1) / LM_BN; }
 
 }  // namespace
 
@@ -786,6 +788,7 @@ int create_plan(void **handle, const QwenBatchedLayer *layers, int num_layers, c
       if (bn_cfg[i] != 0) rc = qb200_gemm_set_bn(gp[i], bn_cfg[i]);
   }
   if (!rc) rc = qb200_gemm_make_maps(&p->g_lm, p->ws.norm16, embed, max_rows, VOCAB, H, H, H);
+  if (!rc) rc = qb200_gemm_set_bn(&p->g_lm, LM_BN);
   const long long k_rows = static_cast<long long>(p->kg.num_pages) * num_layers * NKV * p->kg.page_tokens;
   if (!rc && k_rows > 0x7fffffffll) rc = fail(10, "KV pool of %lld rows exceeds the tensor-map range", k_rows);
   if (!rc) rc = qb200_encode_f16_2d(&p->tm_k, k_pool, HD, k_rows, HD, HD / 2, CH, 1);
@@ -864,7 +867,8 @@ bool run_proj_slices(Plan *p, int i, const GemmPlan &gp, const GemmArgs &g, floa
 int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, const int *tokens_in,
                 float *norm_out, int max_position, float attn_scale, cudaStream_t st) {
   const Workspace &w = p->ws;
-  const int nb8 = (rows + 7) / 8;
+  // The norm kernels take one warp per row; one-warp CTAs spread the rows
+  // over all SMs (eight rows per CTA put the 256 rows of a step on 32 SMs).
   const int nsplit = max_position / CH + 1;
   const int smem = static_cast<int>(sizeof(AttnSmem)) + 1024;
   // Every kernel of the step is launched as a programmatic dependent of the
@@ -882,7 +886,7 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
   const float *down_part = nullptr;  // slices of the previous layer's down projection
   for (int l = 0; l < p->num_layers; ++l) {
     const QwenBatchedLayer &L = p->layers[l];
-    LAUNCH(input_norm_kernel, dim3(nb8), dim3(256), 0, w.hidden, l == 0 ? p->embed : nullptr,
+    LAUNCH(input_norm_kernel, dim3(rows), dim3(32), 0, w.hidden, l == 0 ? p->embed : nullptr,
            tokens_in, down_part, p->ksplit[3], static_cast<const float *>(w.act),
            static_cast<const __half *>(L.input_norm), w.xn, rows, w.err);
     GemmArgs g{};
@@ -892,7 +896,7 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     g.out = w.qkv;
     g.ldo = QKV;
     if (int rc = run_proj(p, 0, p->g_qkv[l], qb200tc::EPI_F16, g, w.splitk, st)) return rc;
-    LAUNCH(qk_rope_kv_kernel, dim3(rows), dim3(256), 0, static_cast<const __half *>(w.qkv),
+    LAUNCH(qk_rope_kv_kernel, dim3(rows), dim3(32 * (NQ + NKV)), 0, static_cast<const __half *>(w.qkv),
            static_cast<const __half *>(L.q_norm), static_cast<const __half *>(L.k_norm), p->cos_t,
            p->sin_t, seq_ids, positions, p->k_pool, p->v_pool, w.qrot, l, p->kg, p->max_seq,
            p->num_seqs, w.err);
@@ -909,7 +913,7 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     const bool o_sliced = run_proj_slices(p, 1, p->g_o[l], g, w.splitk, st, &rc);
     if (rc) return rc;
     if (!o_sliced && (rc = run_proj(p, 1, p->g_o[l], qb200tc::EPI_F32_RES16, g, w.splitk, st))) return rc;
-    LAUNCH(post_norm_kernel, dim3(nb8), dim3(256), 0, w.act,
+    LAUNCH(post_norm_kernel, dim3(rows), dim3(32), 0, w.act,
            o_sliced ? static_cast<const float *>(w.splitk) : nullptr, p->ksplit[1],
            static_cast<const __half *>(w.hidden), static_cast<const __half *>(L.post_norm), w.sact, rows);
     g.out = w.inter;
@@ -924,7 +928,7 @@ int step_layers(Plan *p, int rows, const int *seq_ids, const int *positions, con
     if (!down_sliced && (rc = run_proj(p, 3, p->g_down[l], qb200tc::EPI_F16_RES32, g, w.splitk, st))) return rc;
     down_part = down_sliced ? w.splitk : nullptr;
   }
-  LAUNCH(final_norm_kernel, dim3(nb8), dim3(256), 0, w.hidden, down_part, p->ksplit[3],
+  LAUNCH(final_norm_kernel, dim3(rows), dim3(32), 0, w.hidden, down_part, p->ksplit[3],
          static_cast<const float *>(w.act), p->final_norm, w.norm16, norm_out, rows);
 #undef LAUNCH
   return 0;
