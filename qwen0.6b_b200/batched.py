@@ -90,7 +90,7 @@ def pack_layer(lw: list) -> dict:
                 w_gu=w_gu, w_down=down.contiguous())
 
 
-PAGE = 128  # tokens per KV page (the attention split length)
+PAGE = 128  # tokens per KV page
 
 
 class PagePool:

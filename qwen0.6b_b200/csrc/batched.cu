@@ -55,7 +55,9 @@ constexpr int H = 1024, IM = 3072, NQ = 16, NKV = 8, HD = 128;
 constexpr int QS = NQ * HD, KVS = NKV * HD, QKV = QS + 2 * KVS;
 constexpr int VOCAB = 151936;
 constexpr float EPS = 1e-6f;
-constexpr int CH = 128;                 // tokens per attention split
+constexpr int PAGE = 128;               // tokens per KV page (paged pools)
+constexpr int CH = 64;                  // tokens per attention split (34 KB of K/V: six CTAs per SM)
+static_assert(PAGE % CH == 0, "a split never crosses a page");
 constexpr int ATT_THREADS = 128;
 constexpr int PART = HD + 2;            // acc[128], m, l per (row, kv head, split, head)
 constexpr long long WAIT_NS = 2000000000LL;
@@ -69,8 +71,8 @@ __device__ __noinline__ void record_err(unsigned long long *err, uint32_t code) 
 }
 
 // KV pool geometry.  Contiguous pools: page = sequence, one page of max_seq
-// tokens per (sequence, layer, kv head).  Paged pools: pages of CH tokens,
-// page_table[seq * max_pages + position / CH] names the page of a position
+// tokens per (sequence, layer, kv head).  Paged pools: pages of PAGE tokens,
+// page_table[seq * max_pages + position / PAGE] names the page of a position
 // (-1: none).  Pool row of (sequence, layer, kv head g, position):
 // ((page * layers + layer) * 8 + g) * page_tokens + position % page_tokens.
 struct KvGeom {
@@ -704,9 +706,9 @@ int create_plan(void **handle, const QwenBatchedLayer *layers, int num_layers, c
   if (num_layers < 1 || num_layers > 64) return fail(10, "num_layers=%d out of range [1, 64]", num_layers);
   if (num_seqs < 1 || max_seq < 1 || max_seq > 65536 || max_rows < 1 || max_rows > 65535 * 8)
     return fail(10, "num_seqs=%d max_seq=%d max_rows=%d out of range", num_seqs, max_seq, max_rows);
-  if (page_table != nullptr && (num_pages < 1 || max_pages < 1 || static_cast<long long>(max_pages) * CH < max_seq))
+  if (page_table != nullptr && (num_pages < 1 || max_pages < 1 || static_cast<long long>(max_pages) * PAGE < max_seq))
     return fail(10, "paged pools: num_pages=%d, max_pages=%d pages of %d tokens must cover max_seq=%d",
-                num_pages, max_pages, CH, max_seq);
+                num_pages, max_pages, PAGE, max_seq);
   for (const void *p : {embed, final_norm, cos_table, sin_table, static_cast<const void *>(k_pool),
                         static_cast<const void *>(v_pool), static_cast<const void *>(workspace)})
     if (p == nullptr || !al16(p)) return fail(14, "pointers must be non-null and 16-byte aligned");
@@ -738,7 +740,7 @@ int create_plan(void **handle, const QwenBatchedLayer *layers, int num_layers, c
   p->kg.num_layers = num_layers;
   p->kg.max_pages = page_table != nullptr ? max_pages : 1;
   p->kg.num_pages = page_table != nullptr ? num_pages : num_seqs;
-  p->kg.page_tokens = page_table != nullptr ? CH : max_seq;
+  p->kg.page_tokens = page_table != nullptr ? PAGE : max_seq;
   carve(static_cast<uint8_t *>(workspace), max_rows, p->max_splits, p->lm_tiles, &p->ws);
   // Tiling of the four projections: tile width (0: by output size), K slices,
   // cluster reduction.  QB200_GEMM_CFG="name:bn:ksplit:cluster,..." (names
