@@ -969,7 +969,7 @@ int qwen_b200_batched_step(void *handle, int rows, const int *seq_ids, const int
   g.ldo = 1;
   g.part_val = w.arg_val;
   g.part_idx = w.arg_idx;
-  if (int rc = qb200_gemm_run(p->g_lm, qb200tc::EPI_ARGMAX, g, st)) return rc;
+  if (int rc = qb200_gemm_run_argmax(p->g_lm, g, st)) return rc;
   if (int rc = qb200_argmax_reduce(w.arg_val, w.arg_idx, p->lm_tiles, rows, tokens_out, st, true))
     return rc;
   const cudaError_t e = cudaGetLastError();

@@ -190,10 +190,15 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mb
       done = true;
     }
   }
-  const dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.k_splits > 1 ? g.k_splits : 1);
+  // B larger than a quarter of L2 (the lm_head's 311 MB): the row tiles of a
+  // column tile are launched next to each other (grid.x), so that the second
+  // row tile reads B from L2 instead of DRAM.
+  const unsigned mt = static_cast<unsigned>((g.M + BM - 1) / BM), nt = static_cast<unsigned>((g.N + BN - 1) / BN);
+  GemmArgs ga = g;
+  ga.m_fast = mt > 1 && nt <= 65535u && static_cast<long long>(g.N) * g.K * 2 > (32ll << 20);
+  const dim3 grid(ga.m_fast ? mt : nt, ga.m_fast ? nt : mt, g.k_splits > 1 ? g.k_splits : 1);
   // One wave of CTAs: the deepest ring; more: a ring half as deep, so that
   // two CTAs share an SM.
-  GemmArgs ga = g;
   const long long ctas = static_cast<long long>(grid.x) * grid.y * grid.z;
   ga.stages = ctas <= 148 ? GemmSmem<BN>::MAX_STAGES : GemmSmem<BN>::MAX_STAGES / 2;
   // The epilogue stages its tiles in the ring.
@@ -238,7 +243,46 @@ int launch_bn_mn(int epi, const GemmPlan &p, const GemmArgs &g, cudaStream_t st)
 
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+bool g_attr_argmax[64][3] = {};  // [device][BN 64/128/256]
+int g_sm_count[64] = {};
+
+template <int BN>
+int launch_argmax(const GemmPlan &p, const GemmArgs &g, cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(2, "cudaGetDevice failed");
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    bool &done = g_attr_argmax[dev][BN == 64 ? 0 : (BN == 128 ? 1 : 2)];
+    if (!done) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_argmax_persistent<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(GemmSmem<BN>::bytes(GemmSmem<BN>::MAX_STAGES)));
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return fail(4, "argmax GEMM set-up: %s", cudaGetErrorString(e));
+      done = true;
+    }
+  }
+  GemmArgs ga = g;
+  ga.stages = GemmSmem<BN>::MAX_STAGES;
+  const long long tiles = static_cast<long long>((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
+  const unsigned grid = static_cast<unsigned>(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
+  const cudaError_t e = qb200_launch(gemm_argmax_persistent<BN>, dim3(grid), dim3(THREADS),
+                                     GemmSmem<BN>::bytes(ga.stages), st, ga.pdl != 0, p.ma, p.mb, ga);
+  if (e != cudaSuccess) return fail(20, "argmax GEMM launch: %s", cudaGetErrorString(e));
+  return 0;
+}
+
 }  // namespace
+
+int qb200_gemm_run_argmax(const GemmPlan &p, GemmArgs g, cudaStream_t st) {
+  if (p.bl != BL_K) return fail(10, "the persistent argmax GEMM takes a K-major B");
+  if (g.part_val == nullptr || g.part_idx == nullptr) return fail(13, "argmax partials missing");
+  g.M = (g.M > 0 && g.M < p.M) ? g.M : p.M;
+  g.N = p.N;
+  g.K = p.K;
+  g.n_tiles = (p.N + p.bn - 1) / p.bn;
+  if (p.bn == 256) return launch_argmax<256>(p, g, st);
+  return p.bn == 128 ? launch_argmax<128>(p, g, st) : launch_argmax<64>(p, g, st);
+}
 
 int qb200_gemm_bn(int M, int N) {
   const long long tiles128 = static_cast<long long>((N + 127) / 128) * ((M + BM - 1) / BM);
@@ -369,7 +413,7 @@ int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, in
   g.part_val = static_cast<float *>(workspace);
   g.part_idx = reinterpret_cast<int *>(g.part_val + static_cast<size_t>(rows) * n_tiles);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (int rc = qb200_gemm_run(p, EPI_ARGMAX, g, st)) return rc;
+  if (int rc = qb200_gemm_run_argmax(p, g, st)) return rc;
   const int wpb = 8;
   argmax_pair_kernel<<<(rows + wpb - 1) / wpb, 32 * wpb, 0, st>>>(g.part_val, g.part_idx, n_tiles,
                                                                  rows, index_offset, out_val, out_idx);

@@ -34,6 +34,9 @@ int qb200_gemm_set_bn(GemmPlan *p, int bn);
 // Launches the GEMM with epilogue `epi` (qb200tc::Epilogue) on the first g.M
 // rows (all planned rows when g.M is 0); g.N/K/n_tiles come from the plan.
 int qb200_gemm_run(const GemmPlan &p, int epi, qb200tc::GemmArgs g, cudaStream_t st);
+// Row argmax partials (EPI_ARGMAX semantics) by the persistent lm_head kernel:
+// one CTA per SM over all tiles, row tiles of a column tile adjacent.
+int qb200_gemm_run_argmax(const GemmPlan &p, qb200tc::GemmArgs g, cudaStream_t st);
 // Split-K: `splits` CTAs along K write fp32 partial slices into `partial`
 // ([splits, M, N]); a reduction sums them in slice order and applies `epi`
 // (EPI_F16, EPI_F32, EPI_F32_RES16 or EPI_F16_RES32) into g.out.

@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(chain_threads<DUAL, SPLIT>())
   }
 }
 
-// RMSNorm, one warp per row (8 rows per 256-thread CTA).  With `res`, the
+// RMSNorm, one warp per row (blockDim / 32 rows per CTA).  With `res`, the
 // fused form: res = half(x + res) written back, then normalise res.
 // Elements below (cols / 4) * 4 follow upstream's vector path, the rest its
 // scalar remainder path (rmsnorm.cuh:47-76, :95-108), whose rounding differs.
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(256)
                    __half *__restrict__ res, long long rows, int cols, float eps) {
   qb200::griddep_wait();
   qb200::griddep_launch_dependents();
-  const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const __half *xr = x + row * cols;
@@ -498,10 +498,13 @@ int rmsnorm_launch(void *out, float *rms, const void *input, const void *weight,
                           static_cast<const void *>(residual)})
       if (q != nullptr && !al16(q)) return fail(14, "RMSNorm operands must be 16-byte aligned");
   }
-  const long long blocks = (rows + 7) / 8;
+  // Up to a few thousand rows: one-warp CTAs, so that the rows spread over
+  // all SMs (eight rows per CTA put 256 rows on 32 SMs); more: eight per CTA.
+  const int wpc = rows >= 8 * 148 ? 8 : 1;
+  const long long blocks = (rows + wpc - 1) / wpc;
   if (blocks > 0x7fffffffll) return fail(10, "rows=%lld too large", rows);
   const cudaError_t e = qb200_launch(
-      rmsnorm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, true,
+      rmsnorm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * wpc), 0, st, true,
       static_cast<__half *>(out), rms, static_cast<const __half *>(input),
       static_cast<const __half *>(weight), static_cast<__half *>(residual), rows, cols, eps);
   if (e != cudaSuccess) return fail(20, "RMSNorm kernel launch: %s", cudaGetErrorString(e));

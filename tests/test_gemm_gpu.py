@@ -239,3 +239,37 @@ def test_swiglu_after_split_k(bn):
         err = (out.float() - want.float()).abs()
         tol = 2 * want.float().abs().clamp_min(6e-5) * 2.0 ** -10 + 2e-3 * up.abs() + 1e-3
         assert not bool((err > tol).any()), float(err.max())
+
+
+@pytest.mark.parametrize("M,N", [(1, 151936), (129, 18992), (256, 151936), (300, 4160)])
+def test_persistent_lm_head_argmax_matches_tile_kernel(M, N):
+    """The lm_head path (qwen_b200_lmhead_argmax: one persistent CTA per SM
+    over all tiles, double-buffered accumulators) gives the same tokens as the
+    one-tile-per-CTA EPI_ARGMAX GEMM, bit for bit (same per-tile MMA order,
+    lowest index among equal values), and the fp32 reference's token where
+    the top two logits are apart.  Shapes: a single row, ragged column tiles
+    (an 8-way vocabulary shard), three row tiles."""
+    K = 1024
+    a, b = _inputs(M, N, K, 41)
+    want = gemm(EPI_ARGMAX, a, b)
+    f = lib().qwen_b200_lmhead_argmax
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_longlong,
+                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    wsz = lib().qwen_b200_lmhead_argmax_workspace
+    wsz.restype = ctypes.c_longlong
+    wsz.argtypes = [ctypes.c_int, ctypes.c_int]
+    ws = torch.empty(max(16, wsz(M, N)), dtype=torch.uint8, device="cuda")
+    val = torch.empty(M, dtype=torch.float32, device="cuda")
+    idx = torch.empty(M, dtype=torch.int32, device="cuda")
+    rc = f(a.data_ptr(), b.data_ptr(), M, N, 0, val.data_ptr(), idx.data_ptr(), ws.data_ptr(),
+           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if rc:
+        raise RuntimeError(last_error())
+    torch.cuda.synchronize()
+    assert torch.equal(idx, want)
+    ref = ref_mm(a, b)
+    top2 = torch.topk(ref, 2, dim=1)
+    sel = (top2.values[:, 0] - top2.values[:, 1]) > 1e-3
+    assert torch.equal(idx.long()[sel], top2.indices[sel, 0])
+    assert torch.allclose(val, ref.gather(1, idx.long().view(-1, 1)).view(-1), atol=2e-3, rtol=2e-3)
