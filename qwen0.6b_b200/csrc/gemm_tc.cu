@@ -194,6 +194,7 @@ int launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mb
   // column tile are launched next to each other (grid.x), so that the second
   // row tile reads B from L2 instead of DRAM.
   const unsigned mt = static_cast<unsigned>((g.M + BM - 1) / BM), nt = static_cast<unsigned>((g.N + BN - 1) / BN);
+  if (g.a_box < 8 || g.a_box > BM || (g.a_box & 7)) return fail(10, "A box of %d rows", g.a_box);
   GemmArgs ga = g;
   ga.m_fast = mt > 1 && nt <= 65535u && static_cast<long long>(g.N) * g.K * 2 > (32ll << 20);
   const dim3 grid(ga.m_fast ? mt : nt, ga.m_fast ? nt : mt, g.k_splits > 1 ? g.k_splits : 1);
@@ -243,6 +244,10 @@ int launch_bn_mn(int epi, const GemmPlan &p, const GemmArgs &g, cudaStream_t st)
 
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Rows per A copy: a whole 128-row tile, or, for fewer planned rows, the rows
+// rounded up to a swizzle atom (8): the tile's other rows are never copied.
+int a_box_rows(int M) { return M >= BM ? BM : ((M + 7) / 8) * 8; }
+
 bool g_attr_argmax[64][3] = {};  // [device][BN 64/128/256]
 int g_sm_count[64] = {};
 
@@ -279,7 +284,9 @@ int qb200_gemm_run_argmax(const GemmPlan &p, GemmArgs g, cudaStream_t st) {
   g.M = (g.M > 0 && g.M < p.M) ? g.M : p.M;
   g.N = p.N;
   g.K = p.K;
+  g.a_box = p.a_box;
   g.n_tiles = (p.N + p.bn - 1) / p.bn;
+  if (g.a_box < 8 || g.a_box > BM || (g.a_box & 7)) return fail(10, "A box of %d rows", g.a_box);
   if (p.bn == 256) return launch_argmax<256>(p, g, st);
   return p.bn == 128 ? launch_argmax<128>(p, g, st) : launch_argmax<64>(p, g, st);
 }
@@ -302,13 +309,15 @@ int qb200_gemm_make_maps(GemmPlan *p, const void *a, const void *b, int M, int N
   p->bn = qb200_gemm_bn(M, N);
   p->b_ptr = b;
   p->ldb = ldb;
-  if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, BM, 1)) return rc;
+  p->a_box = a_box_rows(M);
+  if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, p->a_box, 1)) return rc;
   if (int rc = qb200_encode_f16_2d(&p->mb, b, K, N, ldb, BK, p->bn, 1)) return rc;
   return 0;
 }
 
 int qb200_gemm_run(const GemmPlan &p, int epi, GemmArgs g, cudaStream_t st) {
   g.M = (g.M > 0 && g.M < p.M) ? g.M : p.M;  // fewer rows than planned: the rest stay untouched
+  g.a_box = p.a_box;
   g.N = p.N;
   g.K = p.K;
   g.n_tiles = (p.N + p.bn - 1) / p.bn;
@@ -341,7 +350,8 @@ int qb200_gemm_make_maps_mn(GemmPlan *p, const void *a, const void *b, const voi
   p->K = K;
   p->bn = bn;
   p->bl = b2 != nullptr ? BL_MN2 : BL_MN;
-  if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, BM, 1)) return rc;
+  p->a_box = a_box_rows(M);
+  if (int rc = qb200_encode_f16_2d(&p->ma, a, K, M, lda, BK, p->a_box, 1)) return rc;
   // B stored [K, N] (N contiguous): boxes of 64 columns x BK rows, 128-byte swizzle.
   if (int rc = qb200_encode_f16_2d(&p->mb, b, N, b_rows, ldb, 64, BK, 1)) return rc;
   if (b2 != nullptr) {

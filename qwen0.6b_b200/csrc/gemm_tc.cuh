@@ -93,6 +93,8 @@ struct GemmArgs {
   int lo_col;                   // EPI_SWIGLU2: > 0: also out16[r, lo_col + c] = half(s - half(s))
   int b_kwrap;                  // > 0: B's K coordinate wraps after this many k-blocks
   int m_fast;                   // grid.x walks the row tiles, grid.y the column tiles (set by the launcher)
+  int a_box;                    // rows per A copy (the A map's box height: 128, or M rounded up to 8 when
+                                //   M < 128 -- the slot's other rows only feed accumulator rows >= M)
 };
 
 template <int BN>
@@ -551,6 +553,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   static_assert(BL != BL_MN2 || (BN == 128 && EPI == EPI_SWIGLU2), "gate|up tiles are 64 + 64 columns");
   static_assert(EPI != EPI_SWIGLU2 || BL == BL_MN2, "EPI_SWIGLU2 needs the gate|up B layout");
   const int STAGES = g.stages;
+  const uint32_t stage_tx = static_cast<uint32_t>(g.a_box * BK * 2 + S::B_BYTES);  // bytes landing per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t *full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE);
@@ -620,7 +623,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       for (int kb = 0; kb < pre; ++kb) {
         uint8_t *st = base + kb * S::STAGE;
-        mbar_arrive_expect_tx(&full[kb], S::STAGE);
+        mbar_arrive_expect_tx(&full[kb], stage_tx);
         load_b(st + S::A_BYTES, kb0 + kb, &full[kb]);
       }
       qb200::griddep_wait();
@@ -634,7 +637,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!gemm_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort, g.err, 1)) break;
       if (lane == 0) {
         uint8_t *st = base + s * S::STAGE;
-        mbar_arrive_expect_tx(&full[s], S::STAGE);
+        mbar_arrive_expect_tx(&full[s], stage_tx);
         tma_load_2d(st, &tm_a, (kb0 + kb) * BK, m0, &full[s]);
         load_b(st + S::A_BYTES, kb0 + kb, &full[s]);
       }
@@ -836,6 +839,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                            const GemmArgs g) {
   using S = GemmSmem<BN>;
   const int STAGES = g.stages;
+  const uint32_t stage_tx = static_cast<uint32_t>(g.a_box * BK * 2 + S::B_BYTES);  // bytes landing per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t *full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE);
@@ -886,7 +890,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (lane == 0) {
           uint8_t *st = base + s * S::STAGE;
-          mbar_arrive_expect_tx(&full[s], S::STAGE);
+          mbar_arrive_expect_tx(&full[s], stage_tx);
           tma_load_2d(st, &tm_a, kb * BK, m0, &full[s]);
           tma_load_2d(st + S::A_BYTES, &tm_b, kb * BK, n0, &full[s]);
         }

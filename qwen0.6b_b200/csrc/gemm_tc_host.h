@@ -14,6 +14,7 @@ struct GemmPlan {
   int bl = 0;  // qb200tc::BLayout of B
   const void *b_ptr = nullptr;  // B and its row pitch (K-major plans), to re-encode for another width
   int ldb = 0;
+  int a_box = 128;  // rows per A copy (the A map's box height)
 };
 
 // Tile width (64 or 128 columns) used for an M x N output.
