@@ -402,8 +402,14 @@ int qb200_argmax_reduce(const float *part_val, const int *part_idx, int n_tiles,
 
 extern "C" {
 
+// The lm_head argmax takes 256-column tiles: four N = 256 MMAs per k-block
+// keep the tensor pipe at its peak rate, where N = 128 ones lose ~40 % to the
+// per-k-block commit (103 -> 69 us per 311 MB lm_head at 256 rows, cold).
+constexpr int LMHEAD_BN = 256;
+
 long long qwen_b200_lmhead_argmax_workspace(int rows, int vocab_rows) {
-  return qwen_b200_gemm_argmax_workspace(rows, vocab_rows);
+  if (rows < 1 || vocab_rows < 16) return 0;
+  return static_cast<long long>(rows) * ((vocab_rows + LMHEAD_BN - 1) / LMHEAD_BN) * 8;
 }
 
 int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, int vocab_rows,
@@ -417,6 +423,7 @@ int qwen_b200_lmhead_argmax(const void *hidden, const void *weight, int rows, in
     return fail(10, "index_offset=%lld out of range", index_offset);
   GemmPlan p{};
   if (int rc = qb200_gemm_make_maps(&p, hidden, weight, rows, vocab_rows, 1024, 1024, 1024)) return rc;
+  if (int rc = qb200_gemm_set_bn(&p, LMHEAD_BN)) return rc;
   const int n_tiles = (vocab_rows + p.bn - 1) / p.bn;
   GemmArgs g{};
   g.ldo = 1;
