@@ -459,19 +459,50 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float *__restric
                                                           __half *__restrict__ attn, int max_splits) {
   qb200::griddep_wait();  // everything below reads or overwrites earlier kernels' data
   qb200::griddep_launch_dependents();
+  __shared__ float s_m[HD], s_l[HD];
   const int qh = blockIdx.x, row = blockIdx.y, d = threadIdx.x;
   const int g = qh >> 1, h = qh & 1;
   const int ns = min(max_splits, max(0, (positions[row] + 1 + CH - 1) / CH));
   const float *pp = part + (static_cast<size_t>(row) * NKV + g) * max_splits * 2 * PART + h * PART;
-  float M = -INFINITY;
-  for (int j = 0; j < ns; ++j) M = fmaxf(M, pp[j * 2 * PART + HD]);
   float A = 0.f, L = 0.f;
-  if (M != -INFINITY) {
-    for (int j = 0; j < ns; ++j) {
-      const float mj = pp[j * 2 * PART + HD];
-      const float f = mj == -INFINITY ? 0.f : expf(mj - M);
-      L += pp[j * 2 * PART + HD + 1] * f;
-      A = fmaf(pp[j * 2 * PART + d], f, A);
+  if (ns <= HD) {
+    // Thread j loads split j's (m, l): one round trip for all of them, where
+    // a loop over the splits would wait for each load in turn.
+    if (d < ns) {
+      s_m[d] = pp[d * 2 * PART + HD];
+      s_l[d] = pp[d * 2 * PART + HD + 1];
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int j = 0; j < ns; ++j) M = fmaxf(M, s_m[j]);
+    if (M != -INFINITY) {
+      // Eight splits' acc[d] loaded before their adds; the sums run in split order.
+      for (int j0 = 0; j0 < ns; j0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = j0 + u < ns ? pp[(j0 + u) * 2 * PART + d] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          if (j < ns) {
+            const float mj = s_m[j];
+            const float f = mj == -INFINITY ? 0.f : expf(mj - M);
+            L += s_l[j] * f;
+            A = fmaf(v[u], f, A);
+          }
+        }
+      }
+    }
+  } else {
+    float M = -INFINITY;
+    for (int j = 0; j < ns; ++j) M = fmaxf(M, pp[j * 2 * PART + HD]);
+    if (M != -INFINITY) {
+      for (int j = 0; j < ns; ++j) {
+        const float mj = pp[j * 2 * PART + HD];
+        const float f = mj == -INFINITY ? 0.f : expf(mj - M);
+        L += pp[j * 2 * PART + HD + 1] * f;
+        A = fmaf(pp[j * 2 * PART + d], f, A);
+      }
     }
   }
   const float inv = L > 0.f ? 1.0f / L : 0.f;
