@@ -106,21 +106,40 @@ __device__ __forceinline__ void reduce_down_row(const float *__restrict__ part, 
   const size_t slice4 = static_cast<size_t>(rows) * H / 4;
   const float4 *p4 = reinterpret_cast<const float4 *>(part + static_cast<size_t>(row) * H);
   const float4 *r4 = reinterpret_cast<const float4 *>(res32 + static_cast<size_t>(row) * H);
-  float4 a[8];
+  float4 a[8], r[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = p4[2 * (lane + 32 * (i >> 1)) + (i & 1)];
+  for (int i = 0; i < 8; ++i) r[i] = r4[2 * (lane + 32 * (i >> 1)) + (i & 1)];
+  if (splits <= 4) {
+    // Every slice and the residual requested before the first add (one round
+    // trip); the adds still run in slice order.
+    float4 c[4][8];
+#pragma unroll
+    for (int z = 0; z < 4; ++z)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        c[z][i] = z < splits ? p4[z * slice4 + 2 * (lane + 32 * (i >> 1)) + (i & 1)] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = c[0][i];
+#pragma unroll
+    for (int z = 1; z < 4; ++z)
+      if (z < splits)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = add4(a[i], c[z][i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = p4[2 * (lane + 32 * (i >> 1)) + (i & 1)];
 #pragma unroll 4
-  for (int z = 1; z < splits; ++z) {
-    float4 c[8];
+    for (int z = 1; z < splits; ++z) {
+      float4 c[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) c[i] = p4[z * slice4 + 2 * (lane + 32 * (i >> 1)) + (i & 1)];
+      for (int i = 0; i < 8; ++i) c[i] = p4[z * slice4 + 2 * (lane + 32 * (i >> 1)) + (i & 1)];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = add4(a[i], c[i]);
+      for (int i = 0; i < 8; ++i) a[i] = add4(a[i], c[i]);
+    }
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float4 r0 = r4[2 * (lane + 32 * j)], r1 = r4[2 * (lane + 32 * j) + 1];
-    const float4 x = add4(a[2 * j], r0), y = add4(a[2 * j + 1], r1);
+    const float4 x = add4(a[2 * j], r[2 * j]), y = add4(a[2 * j + 1], r[2 * j + 1]);
     __half2 *h2 = reinterpret_cast<__half2 *>(&v[j]);
     h2[0] = __floats2half2_rn(x.x, x.y);
     h2[1] = __floats2half2_rn(x.z, x.w);
@@ -147,7 +166,9 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   __half *hr = hidden + static_cast<size_t>(row) * H;
-  uint4 v[4];
+  uint4 v[4], wv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) wv[j] = reinterpret_cast<const uint4 *>(w)[lane + 32 * j];  // before the row's loads
   if (embed != nullptr) {
     int tok = tokens[row];
     if (tok < 0 || tok >= VOCAB) {  // recorded; the row decodes token 0 instead of reading out of bounds
@@ -184,9 +205,8 @@ __global__ void __launch_bounds__(256) input_norm_kernel(__half *__restrict__ hi
   __half *o = xn + static_cast<size_t>(row) * H;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const uint4 wv = reinterpret_cast<const uint4 *>(w)[lane + 32 * j];
     const __half2 *h2 = reinterpret_cast<const __half2 *>(&v[j]);
-    const __half2 *w2 = reinterpret_cast<const __half2 *>(&wv);
+    const __half2 *w2 = reinterpret_cast<const __half2 *>(&wv[j]);
     uint4 out;
     __half2 *o2 = reinterpret_cast<__half2 *>(&out);
 #pragma unroll
@@ -525,25 +545,45 @@ __global__ void __launch_bounds__(256) post_norm_kernel(float *__restrict__ act,
   if (row >= rows) return;
   float4 *a4 = reinterpret_cast<float4 *>(act + static_cast<size_t>(row) * H);
   float4 v[8];
+  uint2 wv[8];
   float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) wv[j] = reinterpret_cast<const uint2 *>(w)[lane + 32 * j];  // before the row's loads
   if (part != nullptr) {
-    // Slices as the outer loop: each step issues all eight loads of the lane.
     const size_t slice4 = static_cast<size_t>(rows) * H / 4;
     const float4 *p4 = reinterpret_cast<const float4 *>(part + static_cast<size_t>(row) * H) + lane;
+    uint2 ru[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = p4[32 * j];
+    for (int j = 0; j < 8; ++j) ru[j] = reinterpret_cast<const uint2 *>(res16 + static_cast<size_t>(row) * H)[lane + 32 * j];
+    if (splits <= 4) {
+      // Every slice requested before the first add; the adds run in slice order.
+      float4 c[4][8];
+#pragma unroll
+      for (int z = 0; z < 4; ++z)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[z][j] = z < splits ? p4[z * slice4 + 32 * j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = c[0][j];
+#pragma unroll
+      for (int z = 1; z < 4; ++z)
+        if (z < splits)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = add4(v[j], c[z][j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = p4[32 * j];
 #pragma unroll 4
-    for (int z = 1; z < splits; ++z) {
-      float4 c[8];
+      for (int z = 1; z < splits; ++z) {
+        float4 c[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) c[j] = p4[z * slice4 + 32 * j];
+        for (int j = 0; j < 8; ++j) c[j] = p4[z * slice4 + 32 * j];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = add4(v[j], c[j]);
+        for (int j = 0; j < 8; ++j) v[j] = add4(v[j], c[j]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint2 ru = reinterpret_cast<const uint2 *>(res16 + static_cast<size_t>(row) * H)[lane + 32 * j];
-      const __half2 *r2 = reinterpret_cast<const __half2 *>(&ru);
+      const __half2 *r2 = reinterpret_cast<const __half2 *>(&ru[j]);
       v[j] = add4(v[j], make_float4(__low2float(r2[0]), __high2float(r2[0]), __low2float(r2[1]), __high2float(r2[1])));
       a4[lane + 32 * j] = v[j];
     }
@@ -565,11 +605,12 @@ __global__ void __launch_bounds__(256) post_norm_kernel(float *__restrict__ act,
   for (int j = 0; j < 8; ++j) {
     const int e = 4 * (lane + 32 * j);
     const float x[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    const __half *wj = reinterpret_cast<const __half *>(&wv[j]);  // w[e .. e + 3]
     __half r[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       r[i] = __float2half_rn(
-          __fmul_rn(__fmul_rn(__half2float(__float2half_rn(x[i])), rstd), __half2float(w[e + i])));
+          __fmul_rn(__fmul_rn(__half2float(__float2half_rn(x[i])), rstd), __half2float(wj[i])));
     *reinterpret_cast<uint2 *>(o + e) = *reinterpret_cast<const uint2 *>(r);
   }
 }
