@@ -347,13 +347,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   const size_t krow0 = static_cast<size_t>(krow_s);
   const size_t base = krow0 * HD;
   if (tid == 0) {
+    // The copies go out right after the barriers are initialised (same
+    // thread); the block barrier below publishes both to the other threads.
     mbar_init(&sm.bar_k, 1);
     mbar_init(&sm.bar_v, 1);
     sm.abort = 0;
     qb200::fence_mbar_init();
-  }
-  __syncthreads();
-  if (tid == 0) {
     const uint32_t bytes = static_cast<uint32_t>(ntok) * HD * 2;
     const uint64_t pol = qb200::policy_evict_first();
     // Full boxes: rows past this split's tokens are read too (masked below);
@@ -393,28 +392,41 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_split_kernel(
   float wmax = -INFINITY;
   const int ntile = (ntok + 7) >> 3;
   if (!failed) {
-    for (int tile = warp; tile < ntile; tile += 4) {
-      // Token of this lane's B column; the 8 tokens of a tile sit in different
-      // swizzle rows, so the loads below are bank-conflict free.
-      const int tok = tile * 8 + (lane >> 2);
+    // Two tiles per warp and step (a split holds at most 8 tiles over 4
+    // warps), their MMA chains interleaved; each tile's chain is unchanged.
+    for (int tile = warp; tile < ntile; tile += 8) {
       const __half *kbase = &sm.k[0][0];
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // Token of this lane's B column; the 8 tokens of a tile sit in different
+      // swizzle rows, so the loads below are bank-conflict free.  A second
+      // tile past the split reads rows of the first (results unused).
+      const int tok0 = tile * 8 + (lane >> 2);
+      const int tok1 = tile + 4 < ntile ? tok0 + 32 : tok0;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok, 16 * kk + 2 * (lane & 3)));
-        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok, 16 * kk + 8 + 2 * (lane & 3)));
-        mma16816(d, qa[kk][0], qa[kk][1], b0, b1);
+        const int c0 = 16 * kk + 2 * (lane & 3);
+        const uint32_t b00 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok0, c0));
+        const uint32_t b01 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok0, c0 + 8));
+        const uint32_t b10 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok1, c0));
+        const uint32_t b11 = *reinterpret_cast<const uint32_t *>(kbase + k_swz(tok1, c0 + 8));
+        mma16816(d[0], qa[kk][0], qa[kk][1], b00, b01);
+        mma16816(d[1], qa[kk][0], qa[kk][1], b10, b11);
       }
       if (lane < 8) {
-        const int tt = tile * 8 + 2 * (lane & 3);
-        const float s0 = d[0] * attn_scale, s1 = d[1] * attn_scale;
-        if (tt < ntok) {
-          sm.sc[lane >> 2][tt] = s0;
-          wmax = fmaxf(wmax, s0);
-        }
-        if (tt + 1 < ntok) {
-          sm.sc[lane >> 2][tt + 1] = s1;
-          wmax = fmaxf(wmax, s1);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int tl = tile + 4 * u;
+          if (tl >= ntile) continue;
+          const int tt = tl * 8 + 2 * (lane & 3);
+          const float s0 = d[u][0] * attn_scale, s1 = d[u][1] * attn_scale;
+          if (tt < ntok) {
+            sm.sc[lane >> 2][tt] = s0;
+            wmax = fmaxf(wmax, s0);
+          }
+          if (tt + 1 < ntok) {
+            sm.sc[lane >> 2][tt + 1] = s1;
+            wmax = fmaxf(wmax, s1);
+          }
         }
       }
     }
