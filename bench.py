@@ -33,7 +33,11 @@ independent replicas (one process per GPU) and reports their aggregate.
 GPU, seeded prompt lengths uniform in [32, 512] and uniform token ids,
 prefilled with batched steps (untimed); one bench step = one batched greedy
 step of all 256 sequences (256 tokens).  Sequences are sharded per GPU (seeds
-offset by rank) with no collective; ``value`` is the aggregate tok/s.
+offset by rank) with no collective; ``value`` is the aggregate tok/s.  Its CPU
+figures (``cpu_baseline``: the C oracle; ``cpu_baseline_hf``: HF fp32) decode
+one sequence at the workload's mean position and are marked extrapolated.
+``--workload ops`` also reports ``cpu_baseline_torch``: the same chain as fp32
+torch ops on the host cores.
 ``--impl reference`` times the upstream algorithm's CPU restatement (the C
 oracle, kind "port") with all host threads, rank 0 only; each of its steps is a
 sample of 16 consecutive tokens of config 2's per-token work.
@@ -422,8 +426,38 @@ def batched_line(args, world: int, rank: int, local: int, dev, dist, with_cpu: b
     if rank == 0 and world == 1 and not args.no_cpu_baseline and with_cpu:
         mean_pos = int(statistics.mean(int(p.float().mean()) for p in pos_list))
         line["cpu_baseline"] = batched_cpu_baseline(w_cpu, mean_pos)
+        if not args.no_hf_baseline and args.layers == 28:
+            hf = hf_cpu_baseline(w_cpu, start=mean_pos, seconds=5.0)
+            hf["sample"] = ("one sequence, " + hf["sample"] + f" (batched workload mean position {mean_pos}); "
+                            "extrapolated to the batch: the CPU decodes the sequences one after another")
+            hf["extrapolated"] = True
+            line["cpu_baseline_hf"] = hf
     bd.close()
     return line
+
+
+def torch_ops_cpu_baseline(x, w, wg, wu, wd, eps: float, seconds: float = 5.0) -> dict:
+    """The config-3 chain as fp32 torch ops on the host cores: RMSNorm, then
+    silu(x Wg) * (x Wu) and the down projection (weights in the upstream
+    [H, I] / [I, H] layout), a bounded sample of calls."""
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    xf, wf, g, u, d = (t.float() for t in (x, w, wg, wu, wd))
+
+    def call():
+        xn = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf
+        return (torch.nn.functional.silu(xn @ g) * (xn @ u)) @ d
+
+    call()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 3:
+        call()
+        n += 1
+    dt = time.perf_counter() - t0
+    rows = x.shape[0]
+    return {"value": rows * n / dt, "unit": "rows/s", "cores": threads, "torch_threads": torch.get_num_threads(),
+            "kind": "torch-fp32",
+            "sample": f"{n} calls of RMSNorm + SwiGLU + down projection as fp32 torch ops on {rows} rows ({dt:.1f} s)"}
 
 
 def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
@@ -536,6 +570,7 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
         line["cpu_baseline"] = {"value": B * n / dt, "unit": "rows/s", "cores": threads, "kind": "port",
                                 "sample": f"{n} calls of the C restatement (same fp16 chain) on {B} rows "
                                           f"({dt:.1f} s)"}
+        line["cpu_baseline_torch"] = torch_ops_cpu_baseline(xs, ws_, wgc, wuc, wdc, eps)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -933,7 +968,7 @@ def main() -> None:
         torch.cuda.empty_cache()
         b = batched_line(args, world, rank, local, dev, dist, with_cpu=True)
         keep = ("value", "unit", "ms_per_step", "steps", "warmup", "scaling", "config", "roofline",
-                "e2e", "gpu_launches", "clocks", "cpu_baseline")
+                "e2e", "gpu_launches", "clocks", "cpu_baseline", "cpu_baseline_hf")
         line["batched"] = {k: b[k] for k in keep if k in b}
         torch.cuda.empty_cache()
         # Config 5 (vocabulary-sharded lm_head, B = 256) at the same N.
