@@ -192,6 +192,11 @@ struct __align__(128) Smem {
   float cmb_f[2][MAX_SPLITS];                        // split rescale factor exp(m_j - M) per head
   uint32_t rowaddr[MAX_TILES * 16];  // smem address of each GEMV stage row (padding rows -> row 0)
   int rowinfo[MAX_TILES * 16];       // matrix row | kind << 24
+  // Stage A's row plan (made once per launch, see plan_rows_a):
+  uint32_t plan_po[MAX_TILES * 16];  // stage row -> piece << 16 | byte offset in the piece (~0: padding)
+  int plan_info[MAX_TILES * 16];     // stage row -> matrix row | kind << 24 (-1: padding)
+  int plan_np, plan_total;           // stage A's pieces and rows
+  int plan_o_lo, plan_o_n;           // this CTA's o_proj / down rows (layer 0 copies their embedding)
   const __half *ntab[NTAB_LAYERS][4];  // norm weights of the first layers: input, q, k, post
   float mred[NCW][MAX_TILES * 16];   // per-warp partial dot products
   unsigned long long trace_fullwait;
@@ -817,15 +822,63 @@ __device__ __forceinline__ float block_sum(Smem &sm, float v, bool pred, bool *a
   return t;
 }
 
+// Stage A's row table, planned once per launch.  Its input (the hidden words
+// of the previous layer's stage E) is ready a few hundred ns after the stage
+// starts, so walking the pieces there (qkv_geom + prep_rows, ~0.7 us measured
+// on B200) sat on the critical path.  The other GEMV stages start well before
+// their inputs arrive and keep prep_rows: planning them too made the kernel
+// slower (3-5 %), their handoff polls then starting earlier and loading the
+// memory system while the producing stage still ran.
+// Thread j (< MAX_TILES*16) records which piece holds stage row j, the row's
+// byte offset in it, and its matrix row and kind (padding: row 0 of piece 0).
+__device__ __forceinline__ void plan_rows_a(Smem &sm, int C, int c) {
+  const QkvGeom qg = qkv_geom(C, c);
+  const LayerPtrs lp{};  // consumers only need row ranges, not addresses
+  const int j = threadIdx.x;
+  int total = 0;
+  uint32_t po = ~0u;
+  int info = -1;
+  for (int i = 0; i < qg.total; ++i) {
+    const Piece P = qkv_piece(qg, lp, i);
+    if (po == ~0u && j < total + P.nrows) {
+      po = (static_cast<uint32_t>(i) << 16) | static_cast<uint32_t>((j - total) * 2 * H);
+      info = (P.row0 + (j - total)) | (P.kind << 24);
+    }
+    total += P.nrows;
+  }
+  if (j < MAX_TILES * 16) {
+    sm.plan_po[j] = po;
+    sm.plan_info[j] = info;
+  }
+  if (j == 0) {
+    const Rows o = rows_of(H, C, c);
+    sm.plan_np = qg.total;
+    sm.plan_total = total;
+    sm.plan_o_lo = o.lo;
+    sm.plan_o_n = o.n;
+  }
+}
+
+// prep_rows for stage A from its plan, pieces starting at ring piece n.
+__device__ __forceinline__ int prep_rows_a(Smem &sm, uint32_t n) {
+  const int j = threadIdx.x;
+  if (j < MAX_TILES * 16) {
+    const uint32_t po = sm.plan_po[j];
+    const uint32_t piece = po == ~0u ? 0u : (po >> 16), off = po == ~0u ? 0u : (po & 0xffffu);
+    sm.rowaddr[j] = smem_u32(sm.ring[0]) + ((n + piece) % NSLOTS) * SLOT_BYTES + off;
+    sm.rowinfo[j] = sm.plan_info[j];
+  }
+  return sm.plan_total;
+}
+
 // ---------------------------------------------------------------- stage A
 // Input RMSNorm (megakernel.cu:806-847) + fused QKV GEMV (:242-291).
 __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const WaitCtx &w, St &st,
                                         int l, int token, uint32_t ep, unsigned long long *tr) {
-  const int tid = threadIdx.x, C = gridDim.x, c = blockIdx.x;
+  const int tid = threadIdx.x;
   trace_mark(tr, TR_A0);
-  const QkvGeom qg = qkv_geom(C, c);
-  const LayerPtrs lp{};  // consumers only need row ranges, not addresses
-  const int total = prep_rows<H>(sm, st.n, qg.total, [&](int i) { return qkv_piece(qg, lp, i); });
+  const int np = sm.plan_np;
+  const int total = prep_rows_a(sm, st.n);
   // Norm weights: loaded now, converted only where they are used (after the
   // hidden-vector gather), so their latency hides behind the gather.
   const __half *nw = norm_ptr(sm, a, l, 0);
@@ -833,7 +886,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
   float h[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) wr[i] = __ldg(nw + tid + NCT * i);
-  st.fail |= !wait_pieces(sm, w, st.n, qg.total, W_A);
+  st.fail |= !wait_pieces(sm, w, st.n, np, W_A);
   if (tr != nullptr) {
     __syncwarp();
     trace_mark(tr, TR_A_PIECES);
@@ -842,8 +895,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
     const __half *emb = a.embed + static_cast<size_t>(token) * H;
 #pragma unroll
     for (int i = 0; i < 4; ++i) h[i] = __half2float(__ldg(emb + tid + NCT * i));
-    const Rows o = rows_of(H, C, c);
-    if (tid < o.n) sm.hid_own[tid] = __ldg(emb + o.lo + tid);
+    if (tid < sm.plan_o_n) sm.hid_own[tid] = __ldg(emb + sm.plan_o_lo + tid);
   } else {
     uint32_t u[4];
     st.fail |= !ll_gather<4>(w, [&](int i) { return a.ws.hidden + tid + NCT * i; }, ep - 1, u, W_A);
@@ -863,7 +915,7 @@ __device__ __forceinline__ bool stage_a(Smem &sm, const DecodeArgs &a, const Wai
   for (int i = 0; i < 4; ++i) sm.xa[tid + NCT * i] = __float2half(h[i] * (inv * __half2float(wr[i])));
   named_bar_sync(BAR_ID, NCT);
   gemv_wr<H, 32>(
-      sm, st.n, qg.total, total, sm.xa,
+      sm, st.n, np, total, sm.xa,
       [&](int kind, int row, float dot) {
         const __half hv = __float2half(dot);
         const int vrow = (kind == 0 ? 0 : (kind == 1 ? QS : QS + KVS)) + row;
@@ -1536,6 +1588,7 @@ __device__ __forceinline__ void consumer(const DecodeArgs &a, Smem &sm) {
   }
   for (int i = threadIdx.x; i < min(L, NTAB_LAYERS) * 4; i += NCT)
     sm.ntab[i >> 2][i & 3] = layer_ptr(a.layers, i >> 2, norm_slot(i & 3));
+  plan_rows_a(sm, C, c);
   named_bar_sync(BAR_ID, NCT);
   int s = 0;
   for (s = 0; s < a.num_steps; ++s) {
