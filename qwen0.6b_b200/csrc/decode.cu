@@ -952,53 +952,47 @@ __device__ __forceinline__ bool stage_b(Smem &sm, const DecodeArgs &a, const Wai
       snv[it] = __ldg(sinp + ri);
     }
   }
-  {
-    uint32_t u[2];
-    st.fail |= !ll_gather<2>(
-        w,
-        [&](int i) {
-          const int t2 = tid + NCT * i;
-          const int word = t2 < 256 ? (256 * g + t2)
-                                    : (t2 < 384 ? (QS + 128 * g + t2 - 256) : (QS + KVS + 128 * g + t2 - 384));
-          return a.ws.qkv + word;
-        },
-        ep, u, W_B);
-    sm.qkv_raw[tid] = u2h(u[0]);
-    sm.qkv_raw[tid + NCT] = u2h(u[1]);
-    if (tid < 2) {
-      sm.att_m[tid] = -INFINITY;
-      sm.att_l[tid] = 0.f;
+  // Warp 0 / 1 gathers q head 2g / 2g+1 and rotates it right away; on the
+  // split that holds the new token, warp 2 also takes k head g (rotated into
+  // k_fresh) and warp 3 v head g (raw).  Other splits read no k / v words.
+  if (tid < 2) {
+    sm.att_m[tid] = -INFINITY;
+    sm.att_l[tid] = 0.f;
+  }
+  if (warp < 2 || (ag.last && warp < 4)) {
+    const int word0 = warp < 2 ? HD * (2 * g + warp) : (warp == 2 ? QS + HD * g : QS + KVS + HD * g);
+    uint32_t u[4];
+    st.fail |= !ll_gather<4>(w, [&](int it) { return a.ws.qkv + word0 + lane + 32 * it; }, ep, u, W_B);
+    if (warp == 3) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) sm.qkv_raw[3 * HD + lane + 32 * it] = u2h(u[it]);
+    } else {
+      // q/k RMSNorm (eps 1e-6) + rotate-half RoPE, megakernel.cu:345-434.
+      float xv[4], ss = 0.f;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        xv[it] = __half2float(u2h(u[it]));
+        ss = fmaf(xv[it], xv[it], ss);
+      }
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
+      float vals[4];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), __half2float(nwv[it]));
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int i = lane + 32 * it;
+        const float c = __half2float(csv[it]), sn = __half2float(snv[it]);
+        const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], c), __fmul_rn(vals[it + 2], sn))
+                               : __fadd_rn(__fmul_rn(vals[it - 2], sn), __fmul_rn(vals[it], c));
+        const __half hr = __float2half(r);
+        if (warp < 2) sm.q_rot[warp][i] = hr;
+        else sm.k_fresh[i] = hr;
+      }
     }
   }
   if (named_bar_or(BAR_ID, NCT, st.fail || sm.abort)) return true;
   trace_mark(tr, TR_B1);
-
-  // q/k RMSNorm (eps 1e-6) + rotate-half RoPE, megakernel.cu:345-434.
-  if (rope_warp) {
-    const __half *src = sm.qkv_raw + warp * HD;
-    float xv[4], ss = 0.f;
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      xv[it] = __half2float(src[lane + 32 * it]);
-      ss = fmaf(xv[it], xv[it], ss);
-    }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / static_cast<float>(HD) + 1e-6f);
-    float vals[4];
-#pragma unroll
-    for (int it = 0; it < 4; ++it) vals[it] = __fmul_rn(__fmul_rn(xv[it], inv), __half2float(nwv[it]));
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int i = lane + 32 * it;
-      const float c = __half2float(csv[it]), sn = __half2float(snv[it]);
-      const float r = it < 2 ? __fsub_rn(__fmul_rn(vals[it], c), __fmul_rn(vals[it + 2], sn))
-                             : __fadd_rn(__fmul_rn(vals[it - 2], sn), __fmul_rn(vals[it], c));
-      const __half hr = __float2half(r);
-      if (warp < 2) sm.q_rot[warp][i] = hr;
-      else sm.k_fresh[i] = hr;
-    }
-  }
-  named_bar_sync(BAR_ID, NCT);
 
   // A fragments of q (m16n8k16, rows 0/1 = the two q heads, other rows 0).
   // The k order of the MMAs is a permutation of the 128 dims that matches the
