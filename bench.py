@@ -420,7 +420,7 @@ def batched_line(args, world: int, rank: int, local: int, dev, dist, with_cpu: b
                      "algorithmic_bytes_per_step": avg_alg, "avg_step_ms": avg_step_s * 1000.0},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 3 * 4 * n,
                 "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": args.steps * (args.layers * 11 + 3),
+        "gpu_launches": args.steps * (args.layers * 9 + 3),  # 9 kernels per layer, 3 per step
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline and with_cpu:
@@ -551,7 +551,7 @@ def run_ops(args, world: int, rank: int, local: int, dev, dist) -> None:
                               "the serial fp16 chains (1024 + 3072 dependent adds) bound small batches")},
         "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": B * 2048,
                 "d2h_bytes_per_step": B * 2048},
-        "gpu_launches": steps * 3,
+        "gpu_launches": steps * (4 if tc else 3),  # RMSNorm, gate|up, down (+ split-K reduction on the tensor cores)
         "clocks": clk,
     }
     if tc:
